@@ -1,0 +1,154 @@
+/*
+ * ocelotl_cuda.h -- C ABI of the B200 (sm_100a) quantized-linear backend.
+ *
+ * This is the drop-in boundary for Ocelotl's quantized linear-layer hot path.
+ * A host-side backend (the Rust `CudaKernelBackend` a maintainer would add to
+ * `ocelotl-kernels`, or the Python mirror in ocelotl_b200/backend.py) binds these
+ * entry points.  Plain pointers and sizes only; device pointers are CUDA device
+ * addresses on the context's device; `stream` arguments are cudaStream_t passed as
+ * void* (NULL = the context's stream).
+ *
+ * Error convention (crates/core/src/lib.rs:14-30,75-80 and
+ * crates/kernels/src/lib.rs:2443-2494): every call returns OCL_OK (0) or a
+ * negative status.  OCL_ERR_UNSUPPORTED maps to OcelotlError::Unsupported and is
+ * returned BEFORE any launch (unknown ggml type, K not a multiple of the block
+ * size); OCL_ERR_INVALID maps to OcelotlError::Kernel for shape / length / null
+ * pointer mismatches; OCL_ERR_CUDA and OCL_ERR_OOM map to OcelotlError::Kernel
+ * with backend "cuda-sm100a".  ocl_last_error() returns the message of the last
+ * failing call on that context (thread-safe per context).
+ *
+ * Thread safety: the reference trait is Send + Sync (crates/kernels/src/lib.rs:84);
+ * a context serialises its calls with a mutex, so one context may be shared
+ * across host threads.  Use one context per stream for concurrency.
+ */
+#ifndef OCELOTL_CUDA_H
+#define OCELOTL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OCL_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define OCL_API __attribute__((visibility("default")))
+#else
+#define OCL_API
+#endif
+
+/* Status codes. */
+enum {
+    OCL_OK = 0,
+    OCL_ERR_INVALID = -1,     /* shape / length / pointer mismatch -> KernelError */
+    OCL_ERR_UNSUPPORTED = -2, /* type / shape outside the supported set -> Unsupported */
+    OCL_ERR_CUDA = -3,        /* CUDA runtime failure -> KernelError */
+    OCL_ERR_OOM = -4,         /* device allocation failed -> KernelError */
+    OCL_ERR_TIMEOUT = -5      /* a bounded device-side wait gave up -> KernelError */
+};
+
+/* GGUF tensor-type tags, crates/loader/src/gguf_inspect.rs:178,182,184. */
+enum { OCL_Q8_0 = 8, OCL_Q4_K = 12, OCL_Q6_K = 14 };
+
+/* Device layouts of a quantized weight.
+ *  OCL_LAYOUT_GGUF:    the GGUF super-blocks as stored in the file, row-major
+ *                      [n_rows, k/block_elems] blocks (input format only).
+ *  OCL_LAYOUT_TILED16: the repacked layout every kernel reads: 16-row tiles, each
+ *                      tile's blocks regrouped so that one coalesced 16-byte load
+ *                      per lane yields tensor-core operand fragments (the exact byte
+ *                      map is documented in ocelotl_b200/csrc/layout.cuh).  Same byte
+ *                      count as GGUF for N a multiple of 16. */
+enum { OCL_LAYOUT_GGUF = 0, OCL_LAYOUT_TILED16 = 1 };
+
+typedef struct ocl_ctx ocl_ctx;   /* one device + stream + scratch */
+typedef struct ocl_qbuf ocl_qbuf; /* a quantized weight resident in HBM */
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Create a context on CUDA device `device` (Device::Gpu{ordinal},
+ * crates/core/src/lib.rs:437-441).  Replaces the backend construction done in
+ * crates/kernels/src/cubecl_backend.rs:46-69 for the CubeCL backend. */
+OCL_API int ocl_cuda_init(int device, ocl_ctx** out);
+OCL_API void ocl_cuda_destroy(ocl_ctx* ctx);
+/* Message of the last failing call on `ctx` ("" if none).  With ctx == NULL,
+ * the message of the last failing ocl_cuda_init on this thread. */
+OCL_API const char* ocl_last_error(const ocl_ctx* ctx);
+/* Set the stream later calls launch on (NULL = legacy default stream). */
+OCL_API int ocl_set_stream(ocl_ctx* ctx, void* stream);
+OCL_API int ocl_synchronize(ocl_ctx* ctx);
+/* Backend id used in KernelError{backend}: "cuda-sm100a". */
+OCL_API const char* ocl_backend_id(void);
+OCL_API int ocl_abi_version(void);
+
+/* ---- quantized weights (DeviceBuffer for a quantized tensor) ------------ */
+
+/* Upload `n_rows` rows of `k` weights stored as GGUF blocks of `ggml_type`
+ * (host memory, `layout` = OCL_LAYOUT_GGUF) and repack them on the device into
+ * OCL_LAYOUT_TILED16.  This is the payload upload that the GGUF loader feeds
+ * (crates/loader/src/gguf_inspect.rs:119-130 gives file_offset/byte_len; the
+ * reference stops at the header).  Owns the device allocation until
+ * ocl_q_free (the Rust Drop of CudaQuantBuffer). */
+OCL_API int ocl_q_upload(ocl_ctx* ctx, int ggml_type, const void* host_blocks, size_t n_rows, size_t k,
+                 int layout, ocl_qbuf** out);
+/* Same, from GGUF blocks already in device memory (no host copy). */
+OCL_API int ocl_q_upload_device(ocl_ctx* ctx, int ggml_type, const void* dev_blocks, size_t n_rows,
+                        size_t k, ocl_qbuf** out);
+OCL_API int ocl_q_free(ocl_qbuf* w);
+/* Shape and size of a resident weight.  len_f32 = n_rows * k (DeviceBuffer::len_f32,
+ * crates/kernels/src/tensor.rs:45-68). */
+OCL_API int ocl_q_info(const ocl_qbuf* w, int* ggml_type, size_t* n_rows, size_t* k, size_t* device_bytes);
+/* Device address of the repacked bytes (for callers that rotate copies). */
+OCL_API const void* ocl_q_device_ptr(const ocl_qbuf* w);
+
+/* Dequantize to f32 [n_rows, k] in device memory; bit-exact with the GGUF
+ * block arithmetic.  Backs DeviceBuffer::to_host for a quantized buffer. */
+OCL_API int ocl_q_dequant(ocl_ctx* ctx, const ocl_qbuf* w, float* out_dev);
+/* Write the weight back out as GGUF blocks (host memory): a round trip of the
+ * repacked layout. */
+OCL_API int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_blocks);
+
+/* ---- the hot path -------------------------------------------------------- */
+
+/* y[r, o] = bias[o] + sum_k x[r, k] * W[o, k], x f32 [rows, in_features],
+ * y f32 [rows, out_features], bias f32 [out_features] or NULL; all device
+ * pointers.  W is the resident quantized weight with n_rows == out_features and
+ * k == in_features.  Replaces KernelBackend::linear_d for a quantized weight
+ * (crates/kernels/src/lib.rs:193-217) and, via ocl_q_linear_host, the slice form
+ * linear_out_by_in (crates/kernels/src/lib.rs:107-116, 1939-1967).
+ * rows 1..16 run the dequant-GEMV (HBM-bound); larger `rows` are processed in
+ * 16-row groups by the same kernel.  Accuracy: the products of the integer
+ * quants with x are computed exactly (x split into three int8 planes per 256-k
+ * block, i.e. ~21 significant bits), scaled and accumulated in f32; max relative
+ * error vs the f32 CPU oracle <= 1e-3. */
+OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, size_t rows,
+                 size_t in_features, size_t out_features, const float* bias_dev, float* y_dev);
+
+/* Same with host buffers (x, bias, y in host memory); copies in, runs, copies out
+ * on the context stream and synchronises.  The slice-based linear_out_by_in. */
+OCL_API int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size_t rows,
+                      size_t in_features, size_t out_features, const float* bias_host,
+                      float* y_host);
+
+/* Prefill: y bf16 [rows, out_features] = x bf16 [rows, in_features] . W^T, f32
+ * accumulate on tcgen05 tensor cores (weights dequantized to bf16 tiles in
+ * shared memory).  Tolerance vs the f32 oracle on the same bf16-rounded x:
+ * 2e-2 relative.  bf16 values are passed as uint16_t bit patterns. */
+OCL_API int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_dev, size_t rows,
+                    size_t in_features, size_t out_features, uint16_t* y_dev);
+
+/* Q8_0 embedding gather: out f32 [n_ids, k] = dequantized rows ids[i] of `table`
+ * (ids int32 in device memory), bit-exact with the GGUF block arithmetic.  The
+ * ids are only known on the device, so an id outside [0, n_rows) cannot fail the
+ * call without a synchronisation: its row is written as zeros and a per-context
+ * device counter is bumped; ocl_take_bad_ids reads and clears that counter
+ * (synchronising the stream). */
+OCL_API int ocl_q_embed_rows(ocl_ctx* ctx, const ocl_qbuf* table, const int32_t* ids_dev, size_t n_ids,
+                     float* out_dev);
+OCL_API int ocl_take_bad_ids(ocl_ctx* ctx, unsigned int* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,307 @@
+"""Host-side mirror of the reference's `KernelBackend` for quantized weights.
+
+`CudaKernelBackend` is what `ocelotl-kernels` would register as its CUDA backend
+(crates/kernels/src/lib.rs:84-495): the same method names, argument meaning and
+error behaviour, for a weight that is a resident GGUF-quantized tensor.  All
+compute goes through the C ABI in include/ocelotl_cuda.h (libocelotl_cuda.so);
+torch is used only to own device memory and streams.
+
+Reference interfaces mirrored:
+  * linear_out_by_in (host slices)    crates/kernels/src/lib.rs:107-116, 1939-1967
+  * linear_d (device-resident)        crates/kernels/src/lib.rs:193-217
+  * upload / alloc                    crates/kernels/src/lib.rs:176-184
+  * DeviceTensor / DeviceBuffer       crates/kernels/src/tensor.rs:45-268
+  * shape validation messages         crates/kernels/src/lib.rs:2443-2494
+  * downcast of the weight buffer     crates/kernels/src/cubecl_backend.rs:245-293, 2413-2439
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .errors import KernelError, UnsupportedError
+from .ggml import GgmlType, byte_len, geometry
+
+BACKEND_ID = "cuda-sm100a"
+
+
+def _kernel_err(message: str) -> KernelError:
+    return KernelError(BACKEND_ID, message)
+
+
+class QuantBuffer:
+    """A GGUF-quantized weight resident in HBM (the CUDA `DeviceBuffer`).
+
+    `len_f32()` is the logical element count (n_rows * k) so the reference's
+    length checks hold; `to_host()` returns the dequantized f32 values, so the
+    trait's default readback path stays correct; `write_from_host` is
+    unsupported for quantized buffers.
+    """
+
+    def __init__(self, backend: "CudaKernelBackend", handle: int, ggml_type: int, n_rows: int, k: int):
+        self._backend = backend
+        self._handle = C.c_void_p(handle)
+        self.ggml_type = GgmlType(ggml_type)
+        self.n_rows = n_rows
+        self.k = k
+
+    # DeviceBuffer surface -------------------------------------------------
+    def backend_id(self) -> str:
+        return BACKEND_ID
+
+    def len_f32(self) -> int:
+        return self.n_rows * self.k
+
+    def to_host(self) -> np.ndarray:
+        return self._backend.dequant(self).cpu().numpy().reshape(-1)
+
+    def write_from_host(self, src) -> None:
+        raise UnsupportedError("write_from_host on a quantized buffer", self.ggml_type.name, ["f32 buffers"])
+
+    # extras -----------------------------------------------------------------
+    @property
+    def handle(self) -> C.c_void_p:
+        if not self._handle:
+            raise _kernel_err("quantized buffer used after free")
+        return self._handle
+
+    def device_bytes(self) -> int:
+        n = C.c_size_t()
+        self._backend._lib.ocl_q_info(self.handle, None, None, None, C.byref(n))
+        return n.value
+
+    def device_ptr(self) -> int:
+        return self._backend._lib.ocl_q_device_ptr(self.handle)
+
+    def to_gguf(self) -> np.ndarray:
+        """The weight written back out as GGUF blocks (layout round trip)."""
+        out = np.empty(byte_len(self.ggml_type, self.n_rows, self.k), dtype=np.uint8)
+        self._backend._check(self._backend._lib.ocl_q_download_gguf(
+            self._backend._ctx, self.handle, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def free(self) -> None:
+        if self._handle:
+            self._backend._lib.ocl_q_free(self._handle)
+            self._handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+@dataclass
+class DeviceTensor:
+    """f32 tensor on host (`numpy`) or device (`torch`, cuda), or a quantized weight."""
+
+    host: np.ndarray | None = None
+    device: torch.Tensor | None = None
+    quant: QuantBuffer | None = None
+
+    @staticmethod
+    def from_host(v) -> "DeviceTensor":
+        return DeviceTensor(host=np.ascontiguousarray(v, dtype=np.float32).reshape(-1))
+
+    def len_f32(self) -> int:
+        if self.quant is not None:
+            return self.quant.len_f32()
+        if self.device is not None:
+            return self.device.numel()
+        return int(self.host.size)
+
+    def to_host_owned(self) -> np.ndarray:
+        if self.quant is not None:
+            return self.quant.to_host()
+        if self.device is not None:
+            return self.device.detach().cpu().numpy().reshape(-1).copy()
+        return self.host.copy()
+
+    def write_from_host_slice(self, src) -> None:
+        src = np.ascontiguousarray(src, dtype=np.float32).reshape(-1)
+        if src.size != self.len_f32():
+            raise _kernel_err(f"write_from_host len {src.size} does not match buffer len {self.len_f32()}")
+        if self.quant is not None:
+            self.quant.write_from_host(src)
+        elif self.device is not None:
+            self.device.copy_(torch.from_numpy(src).view(self.device.shape))
+        else:
+            self.host[:] = src
+
+    def try_as_device_buffer(self):
+        if self.quant is not None:
+            return self.quant
+        if self.device is not None:
+            return self.device
+        raise _kernel_err("tensor is host-resident; expected a device buffer")
+
+
+class CudaKernelBackend:
+    """The B200 (sm_100a) backend for GGUF-quantized linear layers."""
+
+    def __init__(self, device: int = 0):
+        self._lib = _lib.load()
+        ctx = C.c_void_p()
+        rc = self._lib.ocl_cuda_init(device, C.byref(ctx))
+        if rc != _lib.OCL_OK:
+            msg = self._lib.ocl_last_error(None).decode()
+            raise (UnsupportedError("device", message=msg) if rc == _lib.OCL_ERR_UNSUPPORTED else _kernel_err(msg))
+        self._ctx = ctx
+        self.device_index = device
+        self.torch_device = torch.device("cuda", device)
+
+    def __del__(self):
+        try:
+            if self._ctx:
+                self._lib.ocl_cuda_destroy(self._ctx)
+                self._ctx = C.c_void_p()
+        except Exception:
+            pass
+
+    # -- plumbing -------------------------------------------------------------
+    def name(self) -> str:
+        return BACKEND_ID
+
+    def cpu_thread_pool(self):
+        return None
+
+    def _check(self, rc: int) -> None:
+        if rc == _lib.OCL_OK:
+            return
+        msg = self._lib.ocl_last_error(self._ctx).decode()
+        if rc == _lib.OCL_ERR_UNSUPPORTED:
+            raise UnsupportedError("", message=msg)
+        raise _kernel_err(msg)
+
+    def set_stream(self, stream: torch.cuda.Stream | None) -> None:
+        self._check(self._lib.ocl_set_stream(self._ctx, C.c_void_p(stream.cuda_stream if stream else 0)))
+
+    def use_current_stream(self) -> None:
+        """Launch on torch's current stream of this device."""
+        self.set_stream(torch.cuda.current_stream(self.torch_device))
+
+    def synchronize(self) -> None:
+        self._check(self._lib.ocl_synchronize(self._ctx))
+
+    # -- tensors --------------------------------------------------------------
+    def upload(self, host) -> DeviceTensor:
+        a = np.ascontiguousarray(host, dtype=np.float32).reshape(-1)
+        return DeviceTensor(device=torch.from_numpy(a).to(self.torch_device))
+
+    def alloc(self, length: int) -> DeviceTensor:
+        return DeviceTensor(device=torch.zeros(length, dtype=torch.float32, device=self.torch_device))
+
+    def upload_quant(self, ggml_type: int, blocks, n_rows: int, k: int) -> DeviceTensor:
+        """Upload GGUF blocks (host bytes / numpy uint8 / torch uint8 on host or this device)."""
+        geometry(ggml_type)  # Unsupported before anything else
+        expected = byte_len(ggml_type, n_rows, k)
+        h = C.c_void_p()
+        if isinstance(blocks, torch.Tensor) and blocks.is_cuda:
+            if blocks.dtype != torch.uint8 or not blocks.is_contiguous() or blocks.numel() != expected:
+                raise _kernel_err(f"upload_quant blocks must be {expected} contiguous uint8 bytes")
+            self._check(self._lib.ocl_q_upload_device(self._ctx, int(ggml_type), C.c_void_p(blocks.data_ptr()),
+                                                      n_rows, k, C.byref(h)))
+        else:
+            if isinstance(blocks, torch.Tensor):
+                blocks = blocks.numpy()
+            arr = np.frombuffer(blocks, dtype=np.uint8) if isinstance(blocks, (bytes, bytearray)) else \
+                np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+            if arr.size != expected:
+                raise _kernel_err(f"upload_quant blocks len {arr.size} does not match {GgmlType(ggml_type).name} "
+                                  f"[{n_rows}, {k}] = {expected} bytes")
+            self._check(self._lib.ocl_q_upload(self._ctx, int(ggml_type), arr.ctypes.data_as(C.c_void_p),
+                                               n_rows, k, 0, C.byref(h)))
+        return DeviceTensor(quant=QuantBuffer(self, h.value, ggml_type, n_rows, k))
+
+    def dequant(self, w: QuantBuffer) -> torch.Tensor:
+        out = torch.empty(w.n_rows, w.k, dtype=torch.float32, device=self.torch_device)
+        self._check(self._lib.ocl_q_dequant(self._ctx, w.handle, C.c_void_p(out.data_ptr())))
+        self.synchronize()
+        return out
+
+    # -- validation (crates/kernels/src/lib.rs:2443-2494) ----------------------
+    @staticmethod
+    def _validate(x_len, rows, in_features, w_len, out_features, bias_len, out_len, op="linear_out_by_in"):
+        if x_len != rows * in_features:
+            raise _kernel_err(f"{op} x.len()={x_len} does not match rows*in_features="
+                              f"{rows}*{in_features}={rows * in_features}")
+        if w_len != out_features * in_features:
+            raise _kernel_err(f"{op} weight.len()={w_len} does not match out_features*in_features="
+                              f"{out_features}*{in_features}={out_features * in_features}")
+        if bias_len is not None and bias_len != out_features:
+            raise _kernel_err(f"{op} bias.len()={bias_len} does not match out_features={out_features}")
+        if out_len != rows * out_features:
+            raise _kernel_err(f"{op} out.len()={out_len} does not match rows*out_features="
+                              f"{rows}*{out_features}={rows * out_features}")
+
+    @staticmethod
+    def _quant_weight(weight) -> QuantBuffer:
+        q = weight.quant if isinstance(weight, DeviceTensor) else weight
+        if not isinstance(q, QuantBuffer):
+            raise UnsupportedError("linear weight dtype", "f32", ["Q4_K", "Q6_K", "Q8_0 device buffers"])
+        return q
+
+    # -- the hot path -----------------------------------------------------------
+    def linear_d(self, x: DeviceTensor, rows: int, in_features: int, weight: DeviceTensor, out_features: int,
+                 bias: DeviceTensor | None, out: DeviceTensor) -> None:
+        """Device-resident quantized linear: out = x . W^T (+ bias), all on this device."""
+        w = self._quant_weight(weight)
+        self._validate(x.len_f32(), rows, in_features, w.len_f32(), out_features,
+                       None if bias is None else bias.len_f32(), out.len_f32(), op="linear_d")
+        xd, od = x.try_as_device_buffer(), out.try_as_device_buffer()
+        bd = None if bias is None else bias.try_as_device_buffer()
+        for t in (xd, od) + ((bd,) if bd is not None else ()):
+            if not isinstance(t, torch.Tensor) or t.dtype != torch.float32 or not t.is_contiguous() \
+                    or t.device != self.torch_device:
+                raise _kernel_err("linear_d operands must be contiguous f32 tensors on " + str(self.torch_device))
+        self._check(self._lib.ocl_q_linear(self._ctx, w.handle, C.c_void_p(xd.data_ptr()), rows, in_features,
+                                           out_features, C.c_void_p(bd.data_ptr()) if bd is not None else None,
+                                           C.c_void_p(od.data_ptr())))
+
+    def linear_out_by_in(self, x, rows: int, in_features: int, weight, out_features: int, bias, out) -> None:
+        """Host-slice form: x, bias, out are host f32 arrays; weight is resident."""
+        w = self._quant_weight(weight)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if not (isinstance(out, np.ndarray) and out.dtype == np.float32 and out.flags.c_contiguous):
+            raise _kernel_err("linear_out_by_in out must be a contiguous f32 numpy array")
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._validate(x.size, rows, in_features, w.len_f32(), out_features, None if b is None else b.size,
+                       out.size)
+        self._check(self._lib.ocl_q_linear_host(
+            self._ctx, w.handle, x.ctypes.data_as(C.c_void_p), rows, in_features, out_features,
+            b.ctypes.data_as(C.c_void_p) if b is not None else None, out.ctypes.data_as(C.c_void_p)))
+
+    def gemm_bf16(self, x: torch.Tensor, weight, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Prefill: bf16 [rows, in] . W^T -> bf16 [rows, out] on tcgen05 tensor cores."""
+        w = self._quant_weight(weight)
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous() or x.device != self.torch_device:
+            raise _kernel_err("gemm_bf16 x must be a contiguous 2-D bf16 tensor on " + str(self.torch_device))
+        rows, in_features = x.shape
+        if out is None:
+            out = torch.empty(rows, w.n_rows, dtype=torch.bfloat16, device=self.torch_device)
+        if tuple(out.shape) != (rows, w.n_rows) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise _kernel_err(f"gemm_bf16 out must be a contiguous bf16 [{rows}, {w.n_rows}] tensor")
+        self._check(self._lib.ocl_q_gemm_bf16(self._ctx, w.handle, C.c_void_p(x.data_ptr()), rows, in_features,
+                                              w.n_rows, C.c_void_p(out.data_ptr())))
+        return out
+
+    def embed_rows(self, table, ids: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Q8_0 embedding gather of rows `ids` (int32 on this device) -> f32 [len(ids), k]."""
+        w = self._quant_weight(table)
+        if ids.dtype != torch.int32 or not ids.is_contiguous() or ids.device != self.torch_device:
+            raise _kernel_err("embed_rows ids must be a contiguous int32 tensor on " + str(self.torch_device))
+        if out is None:
+            out = torch.empty(ids.numel(), w.k, dtype=torch.float32, device=self.torch_device)
+        self._check(self._lib.ocl_q_embed_rows(self._ctx, w.handle, C.c_void_p(ids.data_ptr()), ids.numel(),
+                                               C.c_void_p(out.data_ptr())))
+        return out
+
+    def take_bad_ids(self) -> int:
+        n = C.c_uint()
+        self._check(self._lib.ocl_take_bad_ids(self._ctx, C.byref(n)))
+        return n.value

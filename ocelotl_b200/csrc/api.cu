@@ -1,0 +1,379 @@
+// api.cu -- the C ABI (include/ocelotl_cuda.h): context, weight upload, the
+// quantized linear entry points.  Host-side validation mirrors
+// validate_linear_out_by_in (crates/kernels/src/lib.rs:2443-2494) and the
+// "unsupported before launch" rule of the reference's kernel design.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ocelotl_cuda.h"
+#include "internal.cuh"
+
+struct ocl_ctx {
+    int device = 0;
+    int sms = 148;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    std::string err;
+    void* scratch = nullptr;  // x planes for the GEMV
+    size_t scratch_bytes = 0;
+    unsigned int* dev_flags = nullptr;  // [0] = bad embedding ids
+};
+
+struct ocl_qbuf {
+    int device = 0;
+    int type = 0;
+    size_t n_rows = 0, k = 0, bytes = 0;
+    void* dev = nullptr;
+};
+
+namespace {
+
+thread_local std::string g_init_err;
+
+int fail(ocl_ctx* ctx, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    else g_init_err = buf;
+    return code;
+}
+
+int cuda_fail(ocl_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, e == cudaErrorMemoryAllocation ? OCL_ERR_OOM : OCL_ERR_CUDA, "%s: %s (%s)", what,
+                cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define OCL_CUDA(ctx, call, what)                                  \
+    do {                                                           \
+        cudaError_t e_ = (call);                                   \
+        if (e_ != cudaSuccess) return cuda_fail((ctx), e_, (what)); \
+    } while (0)
+
+const char* type_name(int t) {
+    return t == OCL_Q4_K ? "Q4_K" : t == OCL_Q6_K ? "Q6_K" : t == OCL_Q8_0 ? "Q8_0" : "?";
+}
+
+// Unsupported type / K before any launch.
+int check_type_k(ocl_ctx* ctx, int type, size_t k) {
+    if (type != OCL_Q4_K && type != OCL_Q6_K && type != OCL_Q8_0)
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `ggml_type` (requested `%d`): supported = [Q4_K(12), Q6_K(14), Q8_0(8)]",
+                    type);
+    const size_t be = (size_t)ocl::block_elems(type);
+    if (k == 0 || k % be != 0)
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `%s in_features` (requested `%zu`): supported = [multiples of %zu]",
+                    type_name(type), k, be);
+    return OCL_OK;
+}
+
+size_t tiled_bytes(int type, size_t n_rows, size_t k) {
+    return (n_rows + 15) / 16 * (k / (size_t)ocl::rec_k(type)) * (size_t)ocl::rec_bytes(type);
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int ensure_scratch(ocl_ctx* ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return OCL_OK;
+    if (ctx->scratch) {
+        // a previous launch may still read the old planes
+        OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        cudaFree(ctx->scratch);
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+    }
+    OCL_CUDA(ctx, cudaMalloc(&ctx->scratch, bytes), "cudaMalloc(scratch)");
+    ctx->scratch_bytes = bytes;
+    return OCL_OK;
+}
+
+int check_linear_shapes(ocl_ctx* ctx, const ocl_qbuf* w, size_t rows, size_t in_features, size_t out_features) {
+    if (!w) return fail(ctx, OCL_ERR_INVALID, "linear_d weight is null");
+    if (w->device != ctx->device)
+        return fail(ctx, OCL_ERR_INVALID, "weight lives on device %d but the context is on device %d", w->device,
+                    ctx->device);
+    if (w->k != in_features)
+        return fail(ctx, OCL_ERR_INVALID, "linear_d weight in_features=%zu does not match in_features=%zu", w->k,
+                    in_features);
+    if (w->n_rows != out_features)
+        return fail(ctx, OCL_ERR_INVALID, "linear_d weight out_features=%zu does not match out_features=%zu",
+                    w->n_rows, out_features);
+    if (rows == 0) return fail(ctx, OCL_ERR_INVALID, "linear_d rows must be > 0");
+    return OCL_OK;
+}
+
+// y = x . W^T (+bias) for device pointers, any rows (16-row groups).
+int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, const float* bias, float* y) {
+    const size_t k = w->k, n = w->n_rows;
+    int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
+    if (rc) return rc;
+    const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
+        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->stream), "x split launch");
+        OCL_CUDA(ctx,
+                 ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, ctx->sms,
+                                  ctx->stream),
+                 "gemv launch");
+    }
+    return OCL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ocl_backend_id(void) { return "cuda-sm100a"; }
+int ocl_abi_version(void) { return OCL_ABI_VERSION; }
+
+int ocl_cuda_init(int device, ocl_ctx** out) {
+    if (!out) return fail(nullptr, OCL_ERR_INVALID, "ocl_cuda_init: out is null");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+    if (device < 0 || device >= count)
+        return fail(nullptr, OCL_ERR_INVALID, "device ordinal %d out of range (%d devices)", device, count);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(nullptr, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `device` (requested `sm_%d%d`): supported = [sm_100a (B200)]", prop.major,
+                    prop.minor);
+    DeviceGuard guard(device);
+    ocl_ctx* ctx = new ocl_ctx();
+    ctx->device = device;
+    ctx->sms = prop.multiProcessorCount;
+    e = cudaMalloc(&ctx->dev_flags, 64);
+    if (e == cudaSuccess) e = cudaMemset(ctx->dev_flags, 0, 64);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(nullptr, e, "context allocation");
+    }
+    *out = ctx;
+    return OCL_OK;
+}
+
+void ocl_cuda_destroy(ocl_ctx* ctx) {
+    if (!ctx) return;
+    {
+        DeviceGuard guard(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        if (ctx->scratch) cudaFree(ctx->scratch);
+        if (ctx->dev_flags) cudaFree(ctx->dev_flags);
+    }
+    delete ctx;
+}
+
+const char* ocl_last_error(const ocl_ctx* ctx) { return ctx ? ctx->err.c_str() : g_init_err.c_str(); }
+
+int ocl_set_stream(ocl_ctx* ctx, void* stream) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->stream = (cudaStream_t)stream;
+    return OCL_OK;
+}
+
+int ocl_synchronize(ocl_ctx* ctx) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return OCL_OK;
+}
+
+static int upload_impl(ocl_ctx* ctx, int type, const void* src, bool src_on_device, size_t n_rows, size_t k,
+                       ocl_qbuf** out) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!out) return fail(ctx, OCL_ERR_INVALID, "ocl_q_upload: out is null");
+    *out = nullptr;
+    int rc = check_type_k(ctx, type, k);
+    if (rc) return rc;
+    if (n_rows == 0) return fail(ctx, OCL_ERR_INVALID, "ocl_q_upload: n_rows must be > 0");
+    if (!src) return fail(ctx, OCL_ERR_INVALID, "ocl_q_upload: blocks pointer is null");
+    DeviceGuard guard(ctx->device);
+    const size_t gguf_bytes = n_rows * (k / (size_t)ocl::block_elems(type)) * (size_t)ocl::block_bytes(type);
+    const size_t bytes = tiled_bytes(type, n_rows, k);
+    ocl_qbuf* w = new ocl_qbuf();
+    w->device = ctx->device;
+    w->type = type;
+    w->n_rows = n_rows;
+    w->k = k;
+    w->bytes = bytes;
+    cudaError_t e = cudaMalloc(&w->dev, bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail(ctx, e, "cudaMalloc(weight)");
+    }
+    const void* dsrc = src;
+    void* staging = nullptr;
+    if (!src_on_device) {
+        e = cudaMalloc(&staging, gguf_bytes);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(staging, src, gguf_bytes, cudaMemcpyHostToDevice, ctx->stream);
+        dsrc = staging;
+    }
+    if (e == cudaSuccess) e = ocl::launch_repack(type, dsrc, (int64_t)n_rows, (int64_t)k, w->dev, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) {
+        cudaFree(w->dev);
+        delete w;
+        return cuda_fail(ctx, e, "weight upload/repack");
+    }
+    *out = w;
+    return OCL_OK;
+}
+
+int ocl_q_upload(ocl_ctx* ctx, int type, const void* host_blocks, size_t n_rows, size_t k, int layout,
+                 ocl_qbuf** out) {
+    if (ctx && layout != OCL_LAYOUT_GGUF) {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `upload layout` (requested `%d`): supported = [GGUF(0)]", layout);
+    }
+    return upload_impl(ctx, type, host_blocks, false, n_rows, k, out);
+}
+
+int ocl_q_upload_device(ocl_ctx* ctx, int type, const void* dev_blocks, size_t n_rows, size_t k, ocl_qbuf** out) {
+    return upload_impl(ctx, type, dev_blocks, true, n_rows, k, out);
+}
+
+int ocl_q_free(ocl_qbuf* w) {
+    if (!w) return OCL_OK;
+    DeviceGuard guard(w->device);
+    if (w->dev) cudaFree(w->dev);
+    delete w;
+    return OCL_OK;
+}
+
+int ocl_q_info(const ocl_qbuf* w, int* type, size_t* n_rows, size_t* k, size_t* device_bytes) {
+    if (!w) return OCL_ERR_INVALID;
+    if (type) *type = w->type;
+    if (n_rows) *n_rows = w->n_rows;
+    if (k) *k = w->k;
+    if (device_bytes) *device_bytes = w->bytes;
+    return OCL_OK;
+}
+
+const void* ocl_q_device_ptr(const ocl_qbuf* w) { return w ? w->dev : nullptr; }
+
+int ocl_q_dequant(ocl_ctx* ctx, const ocl_qbuf* w, float* out_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!w || !out_dev) return fail(ctx, OCL_ERR_INVALID, "ocl_q_dequant: null argument");
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx, ocl::launch_dequant(w->type, w->dev, (int64_t)w->n_rows, (int64_t)w->k, out_dev, ctx->stream),
+             "dequant launch");
+    return OCL_OK;
+}
+
+int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_blocks) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!w || !host_blocks) return fail(ctx, OCL_ERR_INVALID, "ocl_q_download_gguf: null argument");
+    DeviceGuard guard(ctx->device);
+    const size_t bytes = w->n_rows * (w->k / (size_t)ocl::block_elems(w->type)) * (size_t)ocl::block_bytes(w->type);
+    void* tmp = nullptr;
+    OCL_CUDA(ctx, cudaMalloc(&tmp, bytes), "cudaMalloc(download)");
+    cudaError_t e = ocl::launch_unpack(w->type, w->dev, (int64_t)w->n_rows, (int64_t)w->k, tmp, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host_blocks, tmp, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "download");
+    return OCL_OK;
+}
+
+int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, size_t rows, size_t in_features,
+                 size_t out_features, const float* bias_dev, float* y_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_linear_shapes(ctx, w, rows, in_features, out_features);
+    if (rc) return rc;
+    if (!x_dev || !y_dev) return fail(ctx, OCL_ERR_INVALID, "linear_d x/out pointer is null");
+    DeviceGuard guard(ctx->device);
+    return q_linear_locked(ctx, w, x_dev, rows, bias_dev, y_dev);
+}
+
+int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size_t rows, size_t in_features,
+                      size_t out_features, const float* bias_host, float* y_host) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_linear_shapes(ctx, w, rows, in_features, out_features);
+    if (rc) return rc;
+    if (!x_host || !y_host) return fail(ctx, OCL_ERR_INVALID, "linear_out_by_in x/out pointer is null");
+    DeviceGuard guard(ctx->device);
+    const size_t xb = rows * in_features * 4, yb = rows * out_features * 4, bb = bias_host ? out_features * 4 : 0;
+    char* buf = nullptr;
+    OCL_CUDA(ctx, cudaMallocAsync((void**)&buf, xb + yb + bb + 512, ctx->stream), "cudaMallocAsync(io)");
+    float* xd = (float*)buf;
+    float* yd = (float*)(buf + ((xb + 255) & ~(size_t)255));
+    float* bd = bias_host ? (float*)((char*)yd + ((yb + 255) & ~(size_t)255)) : nullptr;
+    cudaError_t e = cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && bd) e = cudaMemcpyAsync(bd, bias_host, bb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) {
+        rc = q_linear_locked(ctx, w, xd, rows, bd, yd);
+        if (rc == OCL_OK) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
+    }
+    cudaFreeAsync(buf, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "linear_out_by_in host path");
+    return OCL_OK;
+}
+
+int ocl_q_embed_rows(ocl_ctx* ctx, const ocl_qbuf* table, const int32_t* ids_dev, size_t n_ids, float* out_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!table || !ids_dev || !out_dev) return fail(ctx, OCL_ERR_INVALID, "embed_rows: null argument");
+    if (table->type != OCL_Q8_0)
+        return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `embedding type` (requested `%s`): supported = [Q8_0]",
+                    type_name(table->type));
+    if (n_ids == 0) return OCL_OK;
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx,
+             ocl::launch_embed(table->dev, (int64_t)table->n_rows, (int64_t)table->k, ids_dev, (int64_t)n_ids, out_dev,
+                               ctx->dev_flags, ctx->stream),
+             "embed launch");
+    return OCL_OK;
+}
+
+int ocl_take_bad_ids(ocl_ctx* ctx, unsigned int* count) {
+    if (!ctx || !count) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx, cudaMemcpyAsync(count, ctx->dev_flags, 4, cudaMemcpyDeviceToHost, ctx->stream), "read flags");
+    OCL_CUDA(ctx, cudaMemsetAsync(ctx->dev_flags, 0, 4, ctx->stream), "clear flags");
+    OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return OCL_OK;
+}
+
+int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_dev, size_t rows, size_t in_features,
+                    size_t out_features, uint16_t* y_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    (void)w; (void)x_dev; (void)rows; (void)in_features; (void)out_features; (void)y_dev;
+    return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `q_gemm_bf16`: supported = []");
+}
+
+}  // extern "C"

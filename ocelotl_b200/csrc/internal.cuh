@@ -1,0 +1,51 @@
+// internal.cuh -- declarations shared by the CUDA translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "layout.cuh"
+
+namespace ocl {
+
+// Activation planes produced by the x-split kernel and read by the GEMV kernels.
+// x[m, k] = xs[m, k/256] * (xq[3m, k] + xq[3m+1, k] / 2^7 + xq[3m+2, k] / 2^14)
+// up to 2^-21 of the block's largest magnitude.  Column c = 3m + s of xq holds
+// split s of activation row m; s16 / s32 hold exact per-16 / per-32 sums of each
+// column (used for the Q6_K "-32" offset and the Q4_K "-dmin*m" term).
+struct XPlanes {
+    int8_t* xq;    // [kColsMax][kx]
+    int32_t* s16;  // [kColsMax][kx/16]
+    int32_t* s32;  // [kColsMax][kx/32]
+    float* xs;     // [kRowsMax][kx/256]
+    int kx;        // K rounded up to a multiple of 256
+};
+
+constexpr int kRowsMax = 16;            // activation rows per GEMV launch
+constexpr int kColsMax = 3 * kRowsMax;  // int8 planes per launch
+
+// Bytes of scratch the x planes need for a given K.
+inline size_t xplanes_bytes(int64_t k) {
+    const int64_t kx = (k + 255) / 256 * 256;
+    return (size_t)kColsMax * kx               // xq
+           + (size_t)kColsMax * (kx / 16) * 4  // s16
+           + (size_t)kColsMax * (kx / 32) * 4  // s32
+           + (size_t)kRowsMax * (kx / 256) * 4 // xs
+           + 4 * 256;                          // alignment slack
+}
+// Carve the planes out of one scratch allocation (256-byte aligned pieces).
+XPlanes xplanes_carve(void* base, int64_t k);
+
+cudaError_t launch_repack(int type, const void* src, int64_t n_rows, int64_t k, void* dst, cudaStream_t s);
+cudaError_t launch_dequant(int type, const void* tiles, int64_t n_rows, int64_t k, float* out, cudaStream_t s);
+cudaError_t launch_unpack(int type, const void* tiles, int64_t n_rows, int64_t k, void* dst, cudaStream_t s);
+cudaError_t launch_embed(const void* tiles, int64_t n_rows, int64_t k, const int32_t* ids, int64_t n_ids,
+                         float* out, unsigned int* bad, cudaStream_t s);
+
+// x [rows<=16, k] f32 -> planes.
+cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, cudaStream_t s);
+// y [rows<=16, n] = planes . W^T (+ bias).  `sms` = SM count of the device.
+cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
+                        const float* bias, float* y, int sms, cudaStream_t s);
+
+}  // namespace ocl
