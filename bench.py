@@ -1,0 +1,433 @@
+"""Benchmark: Llama-3-8B-shaped decoder layer, all linear projections, GGUF-quantized.
+
+Workload: q/k/v fused 4096->6144, o 4096->4096, gate and up
+4096->14336 each (Q4_K), down 14336->4096 (Q6_K); decode batch M (default 1),
+f32 activations N(0,1), seeded random-init weights (synthetic data generated on
+the device).  One step = one pass of the five projections, each its own
+ocl_q_linear call (activation split + fused dequant-GEMV), in the order a
+decoder layer runs them.  The step is captured once per weight copy in a CUDA
+graph; weights rotate over enough distinct copies (>= 4x the 126 MB L2) that
+every step streams its weights from HBM.
+
+metric: algorithmic bytes (quantized weights + f32 activations in + outputs out)
+of the layer / time, GB/s.  With --gpus N (torchrun) the layer runs tensor
+parallel: q/k/v, gate, up split by output rows, o and down split by input
+columns with an NCCL all-reduce of their outputs; total work is fixed
+(strong scaling).
+
+--impl reference times the reference's CPU algorithm (the C restatement in
+oracle/: GGUF dequant + sequential-k f32 linear_out_by_in) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, QKV, FFN = 4096, 6144, 14336
+Q4_K, Q6_K = 12, 14
+# (name, ggml type, out_features, in_features, split): "col" = split rows, "row" = split K
+LAYER = [
+    ("qkv", Q4_K, QKV, HIDDEN, "col"),
+    ("o", Q4_K, HIDDEN, HIDDEN, "row"),
+    ("gate", Q4_K, FFN, HIDDEN, "col"),
+    ("up", Q4_K, FFN, HIDDEN, "col"),
+    ("down", Q6_K, HIDDEN, FFN, "row"),
+]
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210)}
+L2_BYTES = 126 * 2**20
+METRIC = "Q4_K/Q6_K GEMV HBM GB/s (% of 8 TB/s); 8B-shape decode tok/s @1/2/4/8"
+WORKLOAD = "llama3-8b-shape decoder layer, all linear projections (qkv/o/gate/up Q4_K, down Q6_K)"
+KERNELS_PER_CALL = 2  # activation split + GEMV
+
+
+def wbytes(t, n, k):
+    e, b = BLOCK[t]
+    return n * (k // e) * b
+
+
+def proj_bytes(t, n, k, m):
+    return wbytes(t, n, k) + 4 * m * k + 4 * m * n
+
+
+def layer_alg_bytes(m):
+    """Algorithmic bytes of one layer pass (whole job): weights + x in + y out."""
+    return sum(proj_bytes(t, n, k, m) for _, t, n, k, _ in LAYER)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_key):
+    """Per-launch DRAM bytes from the committed ncu summary (None if absent)."""
+    f = ROOT / "profiles" / "gemv_8b_layer_m1.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith(f"dram_bytes_per_launch[{kernel_key}]:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampler running across the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = float(rows[-1][2])
+
+        def pw(r):
+            try:
+                return float(r[3])
+            except ValueError:
+                return 0.0
+        loaded = [s for s, r in zip(sm, rows) if pw(r) > 250.0] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline (oracle/ -- the reference's CPU algorithm)
+# ---------------------------------------------------------------------------
+def cpu_inputs(m, seed):
+    from ocelotl_b200 import synth
+    weights = [synth.quant_blocks(t, n, k, seed, f"cpu.{name}").numpy() for name, t, n, k, _ in LAYER]
+    xs = {name: synth.activations(m, k, seed, f"cpu.x.{name}").numpy() for name, t, n, k, _ in LAYER}
+    return weights, xs
+
+
+def cpu_layer_pass(oracle, weights, xs, m, threads):
+    t0 = time.perf_counter()
+    for (name, t, n, k, _), blocks in zip(LAYER, weights):
+        oracle.q_linear(t, blocks, xs[name], m, k, n, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(m, seed, budget_s=10.0):
+    """Reference CPU path, one thread (the reference's dispatch is serial for rows < 32)."""
+    import oracle
+    oracle.build()
+    weights, xs = cpu_inputs(m, seed)
+    passes, spent = 0, 0.0
+    while spent < budget_s and passes < 50:
+        spent += cpu_layer_pass(oracle, weights, xs, m, 1)
+        passes += 1
+    gbs = layer_alg_bytes(m) * passes / spent / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{passes} full layer passes (5 projections, M={m}) in {spent:.1f}s: GGUF dequant + "
+                      f"sequential-k f32 linear_out_by_in (oracle/oracle.c), 1 thread"}
+
+
+def run_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    weights, xs = cpu_inputs(args.rows, args.seed)
+    for _ in range(args.warmup):
+        cpu_layer_pass(oracle, weights, xs, args.rows, threads)
+    total = sum(cpu_layer_pass(oracle, weights, xs, args.rows, threads) for _ in range(args.steps))
+    gbs = layer_alg_bytes(args.rows) * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init GGUF blocks, N(0,1) activations)",
+        "config": {"workload": WORKLOAD, "rows": args.rows, "host_threads": threads},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"each step = one full layer pass (M={args.rows}): GGUF dequant + sequential-k "
+                                   f"f32 linear_out_by_in restated in C (oracle/), output features split over "
+                                   f"{threads} threads (bit-identical to serial)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def graph_of(fn, be, torch):
+    """Capture fn() into a CUDA graph on a side stream with the backend launching on it."""
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        be.use_current_stream()
+        fn()  # warm: grows the context's scratch outside capture
+        torch.cuda.current_stream().synchronize()
+        with torch.cuda.graph(g, stream=s):
+            be.use_current_stream()
+            fn()
+    be.set_stream(None)
+    torch.cuda.synchronize()
+    return g
+
+
+def run_ocelotl(args):
+    import torch
+    import torch.distributed as dist
+
+    from ocelotl_b200 import synth
+    from ocelotl_b200.backend import CudaKernelBackend
+    from ocelotl_b200.build import build
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local if world > 1 else 0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    if rank == 0:
+        build()
+    if world > 1:
+        dist.barrier()
+    be = CudaKernelBackend(dev.index)
+    m, tp = args.rows, world
+
+    shards = [(name, t, n // tp, k, sp) if sp == "col" else (name, t, n, k // tp, sp) for name, t, n, k, sp in LAYER]
+    sh = {name: (t, n, k, sp) for name, t, n, k, sp in shards}
+    rank_wbytes = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
+    copies = max(2, -(-4 * L2_BYTES // rank_wbytes))
+    weights = []
+    for c in range(copies):
+        ws = {}
+        for name, t, n, k, _ in shards:
+            blocks = synth.quant_blocks(t, n, k, args.seed, f"{name}.r{rank}.c{c}", device=dev)
+            ws[name] = be.upload_quant(t, blocks, n, k)
+            del blocks
+        weights.append(ws)
+    torch.cuda.synchronize()
+    xs = {name: synth.activations(m, k, args.seed, f"x.{name}.r{rank}", device=dev).contiguous()
+          for name, t, n, k, _ in shards}
+    ys = {name: torch.empty(m, n, device=dev, dtype=torch.float32) for name, t, n, k, _ in shards}
+    xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+
+    def step(c):
+        ws = weights[c]
+        for name, t, n, k, sp in shards:
+            be.linear_dev(ws[name], xs[xin[name]], m, ys[name])
+            if sp == "row" and tp > 1:
+                dist.all_reduce(ys[name])
+
+    # ---- device-resident timing: one graph per weight copy --------------------
+    if tp == 1:
+        graphs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
+        run = lambda i: graphs[i % copies].replay()  # noqa: E731
+    else:
+        run = lambda i: step(i % copies)  # noqa: E731  (NCCL inside: eager launches)
+    for i in range(args.warmup):
+        run(i)
+    torch.cuda.synchronize()
+    clocks = Clocks(dev.index)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        run(args.warmup + i)
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t_ = torch.tensor([ms], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms = float(t_.item())
+    ms_step = ms / args.steps
+    gbs = layer_alg_bytes(m) / (ms_step * 1e-3) / 1e9
+
+    # ---- per-projection call time (split + GEMV), graphs of back-to-back calls
+    proj = {}
+    reps = 2 * copies
+    for name, t, n, k, sp in shards:
+        g = graph_of(lambda name=name: [be.linear_dev(weights[r % copies][name], xs[xin[name]], m, ys[name])
+                                        for r in range(reps)], be, torch)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        it = max(3, args.steps // 20)
+        a.record()
+        for _ in range(it):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(b) / (it * reps)
+        pb = proj_bytes(t, n, k, m)
+        proj[name] = {"us": round(us, 3), "GB/s": round(pb / (us * 1e-6) / 1e9, 1), "bytes": pb,
+                      "type": "Q4_K" if t == Q4_K else "Q6_K"}
+    # dominant kernel: the Q4_K GEMV (4 of the 5 calls, ~69% of the bytes)
+    q4 = [p for p in proj if proj[p]["type"] == "Q4_K"]
+    q4_bytes = sum(proj[p]["bytes"] for p in q4)
+    q4_us = sum(proj[p]["us"] for p in q4)
+    ach = q4_bytes / (q4_us * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    roofline = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(ach / peak, 4), "traffic": profile_traffic("q4k") if (tp == 1 and m == 1) else None,
+                "kernel": f"Q4_K split+GEMV calls (qkv, o, gate, up; M={m}), bytes/time summed over the four",
+                "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s"}
+
+    # ---- end to end through the C ABI with host buffers ----------------------
+    pinned_x = {name: xs[name].cpu().pin_memory() for name in xs}
+    pinned_y = {name: torch.empty(m * sh[name][1], dtype=torch.float32).pin_memory() for name in ys}
+    h2d = sum(pinned_x[nm].numel() * 4 for nm in ("qkv", "o", "gate", "down"))
+    d2h = sum(pinned_y[nm].numel() * 4 for nm in pinned_y)
+
+    def e2e_step(i):
+        ws = weights[i % copies]
+        for name, t, n, k, sp in shards:
+            be.linear_out_by_in(pinned_x[xin[name]].numpy(), m, k, ws[name], n, None, pinned_y[name].numpy())
+            if sp == "row" and tp > 1:
+                y = pinned_y[name].to(dev)
+                dist.all_reduce(y)
+                pinned_y[name].copy_(y.cpu())
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t_ = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        e2e_s = float(t_.item())
+    e2e_gbs = layer_alg_bytes(m) * args.steps / e2e_s / 1e9
+
+    # ---- decode batch sweep (configs[1]: M = 1, 2, 4, 8, 16), graphs ----------
+    sweep = {}
+    if args.sweep and tp == 1:
+        for mm in (1, 2, 4, 8, 16):
+            xm = {nm: synth.activations(mm, sh[nm][2], args.seed, f"sx.{nm}", device=dev) for nm in sh}
+            ym = {nm: torch.empty(mm, sh[nm][1], device=dev) for nm in sh}
+
+            def sstep(c, mm=mm, xm=xm, ym=ym):
+                for nm in sh:
+                    be.linear_dev(weights[c][nm], xm[xin[nm]], mm, ym[nm])
+            gs = [graph_of(lambda c=c: sstep(c), be, torch) for c in range(copies)]
+            for i in range(3):
+                gs[i % copies].replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n_it = max(20, args.steps)
+            a.record()
+            for i in range(n_it):
+                gs[i % copies].replay()
+            b.record()
+            torch.cuda.synchronize()
+            us = 1e3 * a.elapsed_time(b) / n_it
+            sweep[str(mm)] = {"layer_us": round(us, 2), "GB/s": round(layer_alg_bytes(mm) / (us * 1e-6) / 1e9, 1),
+                              "tok_s_layer": round(mm / (us * 1e-6), 1)}
+            del gs
+
+    errs = be.take_device_errors()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(m, args.seed, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init GGUF blocks generated on device, N(0,1) activations)",
+            "config": {"workload": WORKLOAD, "rows": m, "parallelism": f"tp{world}",
+                       "l2": f"inputs larger than L2: weights rotate over {copies} distinct copies "
+                             f"({copies * rank_wbytes / 1e6:.0f} MB per GPU, >= 4x the 126 MB L2)",
+                       "alg_bytes_per_step": layer_alg_bytes(m),
+                       "pct_of_8TBps": round(100 * gbs / 8000.0, 2),
+                       "step": "CUDA graph of 5 ocl_q_linear calls" if tp == 1 else "eager calls + NCCL all-reduce"},
+            "roofline": roofline,
+            "projections": proj,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "path": "CudaKernelBackend.linear_out_by_in -> ocl_q_linear_host per projection (pinned host "
+                            "x/y; copies, launches and a stream sync inside every call)"},
+            "gpu_launches": KERNELS_PER_CALL * len(LAYER) * args.steps,
+            "device_errors": {"bad_ids": errs[0], "wait_timeouts": errs[1]},
+            "clocks": clk,
+            "layer_us": round(ms_step * 1e3, 3),
+            "decode_tok_s_layer": round(m / (ms_step * 1e-3), 1),
+        }
+        if sweep:
+            line["m_sweep"] = sweep
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ocelotl", choices=["ocelotl", "reference"])
+    ap.add_argument("--rows", type=int, default=1, help="decode batch M (1..16)")
+    ap.add_argument("--seed", type=int, default=0x0CE107)
+    ap.add_argument("--sweep", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ocelotl(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -78,6 +78,10 @@ OCL_API const char* ocl_last_error(const ocl_ctx* ctx);
 /* Set the stream later calls launch on (NULL = legacy default stream). */
 OCL_API int ocl_set_stream(ocl_ctx* ctx, void* stream);
 OCL_API int ocl_synchronize(ocl_ctx* ctx);
+/* Launch with programmatic dependent launch (default on): a GEMV's weight
+ * stream starts while the previous kernel on the stream finishes; it reads its
+ * activations only after that kernel completed. */
+OCL_API int ocl_set_pdl(ocl_ctx* ctx, int enable);
 /* Backend id used in KernelError{backend}: "cuda-sm100a". */
 OCL_API const char* ocl_backend_id(void);
 OCL_API int ocl_abi_version(void);
@@ -142,11 +146,14 @@ OCL_API int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_d
  * (ids int32 in device memory), bit-exact with the GGUF block arithmetic.  The
  * ids are only known on the device, so an id outside [0, n_rows) cannot fail the
  * call without a synchronisation: its row is written as zeros and a per-context
- * device counter is bumped; ocl_take_bad_ids reads and clears that counter
- * (synchronising the stream). */
+ * device counter is bumped; ocl_take_device_errors reads and clears it. */
 OCL_API int ocl_q_embed_rows(ocl_ctx* ctx, const ocl_qbuf* table, const int32_t* ids_dev, size_t n_ids,
                      float* out_dev);
-OCL_API int ocl_take_bad_ids(ocl_ctx* ctx, unsigned int* count);
+/* Read and clear the context's device-side error counters (synchronises the
+ * stream): embedding ids that were out of range, and bounded device waits that
+ * gave up (a GEMV whose shared-memory stream stalled for ~1 s; its output is
+ * then invalid).  Either pointer may be NULL. */
+OCL_API int ocl_take_device_errors(ocl_ctx* ctx, unsigned int* bad_ids, unsigned int* timeouts);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@ SIGNATURES = {
     "ocl_last_error": (C.c_char_p, [_vp]),
     "ocl_set_stream": (C.c_int, [_vp, _vp]),
     "ocl_synchronize": (C.c_int, [_vp]),
+    "ocl_set_pdl": (C.c_int, [_vp, C.c_int]),
     "ocl_backend_id": (C.c_char_p, []),
     "ocl_abi_version": (C.c_int, []),
     "ocl_q_upload": (C.c_int, [_vp, C.c_int, _vp, _sz, _sz, C.c_int, C.POINTER(_vp)]),
@@ -41,7 +42,7 @@ SIGNATURES = {
     "ocl_q_linear_host": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_gemm_bf16": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "ocl_q_embed_rows": (C.c_int, [_vp, _vp, _vp, _sz, _vp]),
-    "ocl_take_bad_ids": (C.c_int, [_vp, C.POINTER(C.c_uint)]),
+    "ocl_take_device_errors": (C.c_int, [_vp, C.POINTER(C.c_uint), C.POINTER(C.c_uint)]),
 }
 
 _lib = None

@@ -301,7 +301,22 @@ class CudaKernelBackend:
                                                C.c_void_p(out.data_ptr())))
         return out
 
+    def take_device_errors(self) -> tuple[int, int]:
+        """(out-of-range embedding ids, device waits that timed out) since the last call."""
+        bad, tmo = C.c_uint(), C.c_uint()
+        self._check(self._lib.ocl_take_device_errors(self._ctx, C.byref(bad), C.byref(tmo)))
+        return bad.value, tmo.value
+
     def take_bad_ids(self) -> int:
-        n = C.c_uint()
-        self._check(self._lib.ocl_take_bad_ids(self._ctx, C.byref(n)))
-        return n.value
+        return self.take_device_errors()[0]
+
+    def set_pdl(self, enable: bool) -> None:
+        self._check(self._lib.ocl_set_pdl(self._ctx, 1 if enable else 0))
+
+    def linear_dev(self, weight, x: torch.Tensor, rows: int, out: torch.Tensor,
+                   bias: torch.Tensor | None = None) -> None:
+        """linear_d on raw contiguous f32 torch tensors of this device (no checks beyond the C ABI's)."""
+        w = self._quant_weight(weight)
+        self._check(self._lib.ocl_q_linear(self._ctx, w.handle, C.c_void_p(x.data_ptr()), rows, w.k, w.n_rows,
+                                           C.c_void_p(bias.data_ptr()) if bias is not None else None,
+                                           C.c_void_p(out.data_ptr())))

@@ -21,7 +21,12 @@ struct ocl_ctx {
     std::string err;
     void* scratch = nullptr;  // x planes for the GEMV
     size_t scratch_bytes = 0;
-    unsigned int* dev_flags = nullptr;  // [0] = bad embedding ids
+    float* part = nullptr;  // cross-CTA split-K partial sums
+    size_t part_bytes = 0;
+    unsigned int* counters = nullptr;  // split-K arrival counters, zero between launches
+    size_t counter_count = 0;
+    bool pdl = true;  // launch with programmatic dependent launch
+    unsigned int* dev_flags = nullptr;  // [0] bad embedding ids, [1] bounded waits that gave up
 };
 
 struct ocl_qbuf {
@@ -106,6 +111,33 @@ int ensure_scratch(ocl_ctx* ctx, size_t bytes) {
     return OCL_OK;
 }
 
+int ensure_split_buffers(ocl_ctx* ctx, const ocl::GemvPlan& pl) {
+    const size_t pb = pl.part_floats * sizeof(float);
+    if (pb > ctx->part_bytes) {
+        if (ctx->part) {
+            OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+            cudaFree(ctx->part);
+            ctx->part = nullptr;
+            ctx->part_bytes = 0;
+        }
+        OCL_CUDA(ctx, cudaMalloc(&ctx->part, pb), "cudaMalloc(split-K partials)");
+        ctx->part_bytes = pb;
+    }
+    if (pl.ks > 1 && (size_t)pl.groups > ctx->counter_count) {
+        if (ctx->counters) {
+            OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+            cudaFree(ctx->counters);
+            ctx->counters = nullptr;
+            ctx->counter_count = 0;
+        }
+        const size_t cnt = (size_t)pl.groups < 4096 ? 4096 : (size_t)pl.groups;
+        OCL_CUDA(ctx, cudaMalloc(&ctx->counters, cnt * sizeof(unsigned int)), "cudaMalloc(split-K counters)");
+        OCL_CUDA(ctx, cudaMemsetAsync(ctx->counters, 0, cnt * sizeof(unsigned int), ctx->stream), "memset counters");
+        ctx->counter_count = cnt;
+    }
+    return OCL_OK;
+}
+
 int check_linear_shapes(ocl_ctx* ctx, const ocl_qbuf* w, size_t rows, size_t in_features, size_t out_features) {
     if (!w) return fail(ctx, OCL_ERR_INVALID, "linear_d weight is null");
     if (w->device != ctx->device)
@@ -129,10 +161,13 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
     const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
     for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
         const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
-        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->stream), "x split launch");
+        const ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
+        rc = ensure_split_buffers(ctx, pl);
+        if (rc) return rc;
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream), "x split launch");
         OCL_CUDA(ctx,
-                 ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, ctx->sms,
-                                  ctx->stream),
+                 ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, pl, ctx->part,
+                                  ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
                  "gemv launch");
     }
     return OCL_OK;
@@ -180,6 +215,8 @@ void ocl_cuda_destroy(ocl_ctx* ctx) {
         DeviceGuard guard(ctx->device);
         cudaStreamSynchronize(ctx->stream);
         if (ctx->scratch) cudaFree(ctx->scratch);
+        if (ctx->part) cudaFree(ctx->part);
+        if (ctx->counters) cudaFree(ctx->counters);
         if (ctx->dev_flags) cudaFree(ctx->dev_flags);
     }
     delete ctx;
@@ -358,13 +395,23 @@ int ocl_q_embed_rows(ocl_ctx* ctx, const ocl_qbuf* table, const int32_t* ids_dev
     return OCL_OK;
 }
 
-int ocl_take_bad_ids(ocl_ctx* ctx, unsigned int* count) {
-    if (!ctx || !count) return OCL_ERR_INVALID;
+int ocl_take_device_errors(ocl_ctx* ctx, unsigned int* bad_ids, unsigned int* timeouts) {
+    if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
     DeviceGuard guard(ctx->device);
-    OCL_CUDA(ctx, cudaMemcpyAsync(count, ctx->dev_flags, 4, cudaMemcpyDeviceToHost, ctx->stream), "read flags");
-    OCL_CUDA(ctx, cudaMemsetAsync(ctx->dev_flags, 0, 4, ctx->stream), "clear flags");
+    unsigned int h[2] = {0, 0};
+    OCL_CUDA(ctx, cudaMemcpyAsync(h, ctx->dev_flags, 8, cudaMemcpyDeviceToHost, ctx->stream), "read flags");
+    OCL_CUDA(ctx, cudaMemsetAsync(ctx->dev_flags, 0, 8, ctx->stream), "clear flags");
     OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (bad_ids) *bad_ids = h[0];
+    if (timeouts) *timeouts = h[1];
+    return OCL_OK;
+}
+
+int ocl_set_pdl(ocl_ctx* ctx, int enable) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->pdl = enable != 0;
     return OCL_OK;
 }
 

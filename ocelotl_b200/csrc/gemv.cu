@@ -3,21 +3,39 @@
 // y[m, n] = bias[n] + sum_k x[m, k] * W[n, k] with W in TILED16 records.
 //
 // Design (B200, HBM-bound):
-//  * Weights stream from HBM exactly once with coalesced 16-byte loads
-//    (ld.global.nc.L1::no_allocate), one record (16 rows x 256 k) per warp step,
-//    the next record's loads issued before the current one is consumed.
-//  * The GGUF quants are small integers, so the inner products run on the
-//    tensor cores as exact int8 x int8 -> int32 MMAs (mma.sync m16n8k32 /
-//    m16n8k16, ~1.1 POPS on B200): each lane's 16-byte chunk IS its A fragment
-//    (after a nibble mask), no shared-memory staging.  Activations come as three
-//    int8 planes per row (see XPlanes), so the integer sums are exact and the
-//    only rounding happens in the per-super-block f32 scaling:
-//        Q4_K: acc += xs * (d * float(sum_j sc_j*c_j) - dmin * float(sum_j m_j*S_j))
+//  * A tiny split kernel turns x into three int8 planes per row with one
+//    power-of-two scale per 256-k block (x = xs * (p0 + p1/2^7 + p2/2^14),
+//    |error| < 2^-21 of the block max) plus exact per-16 / per-32 plane sums,
+//    once per call, into scratch memory.
+//  * GEMV CTAs of 8 warps = RT row tiles x KW warps per row tile.  Every warp
+//    streams its (row tile, K slice) records through a private two-stage
+//    shared-memory ring filled by bulk asynchronous copies (cp.async.bulk, the
+//    non-tensor TMA path) completing on mbarriers; records are contiguous per
+//    row tile, so one copy moves one 256-k unit (2304 / 3360 / 4352 bytes).
+//    The CTA's slice of the activation planes is bulk-copied into shared memory
+//    once and shared by its warps; the KW partial sums of a row tile are added
+//    in shared memory.
+//  * The GGUF quants are small integers, so the inner products are exact
+//    int8 x int8 -> int32 tensor-core MMAs (mma.sync m16n8k32 / m16n8k16): each
+//    lane's 16-byte chunk of a record IS its A fragment after one mask (the
+//    high Q4_K nibbles run as u8 x s8 at 16x scale).  The only rounding is the
+//    per-super-block f32 scaling:
+//        Q4_K: acc += xs * (d/16 * float(sum_j sc'_j*c_j) - dmin * float(sum_j m_j*S_j))
 //        Q6_K: acc += xs * d * float(sum_j sc_j*(c_j - 32*S_j))
-//        Q8_0: acc += xs * d * float(c)
-//  * K is split across the warps of a CTA (deterministic shared-memory
-//    reduction, fixed order), so a 4096x4096 matrix keeps ~14 warps per SM busy.
+//        Q8_0: acc += xs * sum_b d_b * float(c_b)
+//  * For one activation row the three planes sit in MMA columns 0, 2, 4 so each
+//    lane keeps only its two useful accumulators.
+//  * Narrow matrices also split K across CTAs; those partial sums go through
+//    scratch memory and the last CTA of each row group adds them in split order
+//    (one counter per group).  Every reduction has a fixed order: deterministic.
+//  * Both kernels launch with programmatic dependent launch: the GEMV's weight
+//    stream starts before griddepcontrol.wait, overlapping its predecessors;
+//    planes, partials and counters are touched only after the wait.
+//  * Every mbarrier wait is bounded; a wait that gives up bumps an error counter
+//    the host reads (ocl_take_device_errors), drains its own copies and returns.
 #include <cuda_fp16.h>
+
+#include <cstdlib>
 
 #include "internal.cuh"
 
@@ -25,426 +43,728 @@ namespace ocl {
 
 namespace {
 
-__device__ __forceinline__ uint4 ld_stream(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
+constexpr int kWarps = 8;   // warps per CTA
+constexpr int kStages = 2;  // ring depth per warp
 
-__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                        uint32_t b0, uint32_t b1) {
+__host__ __device__ constexpr int unit_bytes(int t) { return t == kQ4_K ? 2304 : t == kQ6_K ? 3360 : 4352; }
+__host__ __device__ constexpr int sum_per(int t) { return t == kQ4_K ? 8 : t == kQ6_K ? 16 : 0; }
+
+// ---- PTX helpers ------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait with a time limit (~1 s of SM clocks).  Returns false if it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > 2000000000LL) return false;
+    return true;
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_s8_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%10,%10,%10};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-
-__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+__device__ __forceinline__ void mma_u8_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_s8_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
         "{%7,%7,%7,%7};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
         : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
+__device__ __forceinline__ int prmt(uint32_t w, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return (int)r;
+}
+// byte i of w, sign-extended (selector msb = replicate the sign bit)
+__device__ __forceinline__ int sext_byte(uint32_t w, int i) {
+    return prmt(w, (uint32_t)(i | ((8 + i) << 4) | ((8 + i) << 8) | ((8 + i) << 12)));
+}
+// byte i of w, zero-extended (selector 4 picks a byte of the zero operand)
+__device__ __forceinline__ int zext_byte(uint32_t w, int i) {
+    return prmt(w, (uint32_t)(i | (4 << 4) | (4 << 8) | (4 << 12)));
+}
 
 // ---------------------------------------------------------------------------
-// x split: one warp per (row m, 256-k block b).
+// Activation split: x [rows, k] f32 -> three int8 planes per row (global), one
+// warp per (row m, 256-k block b).  Rows past `rows` up to mpad are written as
+// zeros (they feed idle MMA columns).  |x / xs| < 2^7 with xs = 2^e per block.
 // ---------------------------------------------------------------------------
 __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, XPlanes p) {
+    pdl_wait();  // x is the previous kernel's output; planes may still be read by it
+    pdl_trigger();
     const int b = blockIdx.x, m = blockIdx.y, lane = threadIdx.x;
     const int64_t k0 = (int64_t)b * 256 + lane * 8;
     float v[8];
+    if (m < rows && (k & 3) == 0 && k0 + 8 <= k) {
+        const float4 a = *reinterpret_cast<const float4*>(x + (int64_t)m * k + k0);
+        const float4 c = *reinterpret_cast<const float4*>(x + (int64_t)m * k + k0 + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (m < rows && k0 + i < k) ? x[(int64_t)m * k + k0 + i] : 0.0f;
+        for (int i = 0; i < 8; ++i) v[i] = (m < rows && k0 + i < k) ? x[(int64_t)m * k + k0 + i] : 0.0f;
+    }
     float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
     bool finite = true;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) finite = finite && (fabsf(v[i]) <= 3.402823466e38f);
+    for (int i = 0; i < 8; ++i) {
+        amax = fmaxf(amax, fabsf(v[i]));
+        finite = finite && (fabsf(v[i]) <= 3.402823466e38f);
+    }
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     finite = __all_sync(0xffffffffu, finite);
-
-    // amax < 2^E with E the biased exponent - 126; scale so that |v| < 2^7.
+    // amax < 2^E with E = biased exponent - 126; scale so that |v| < 2^7
     int e = 0;
-    if (finite && amax > 0.0f) {
-        const int E = (int)((__float_as_uint(amax) >> 23) & 0xff) - 126;
-        e = max(E - 7, -100);
-    }
+    if (finite && amax > 0.0f) e = max((int)((__float_as_uint(amax) >> 23) & 0xff) - 126 - 7, -100);
     const float scale = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e, exact
-    int8_t q[3][8];
+    uint32_t pk[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    int sum[3] = {0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float s = finite ? v[i] * scale : 0.0f;
-        const float x0 = truncf(s);
-        const float r1 = (s - x0) * 128.0f;
+        const float sv = finite ? v[i] * scale : 0.0f;
+        const float x0 = truncf(sv);
+        const float r1 = (sv - x0) * 128.0f;
         const float x1 = truncf(r1);
-        const float r2 = (r1 - x1) * 128.0f;
-        const float x2 = fminf(fmaxf(rintf(r2), -127.0f), 127.0f);
-        q[0][i] = (int8_t)x0;
-        q[1][i] = (int8_t)x1;
-        q[2][i] = (int8_t)x2;
+        const float x2 = fminf(fmaxf(rintf((r1 - x1) * 128.0f), -127.0f), 127.0f);
+        const int q0 = (int)x0, q1 = (int)x1, q2 = (int)x2;
+        pk[0][i >> 2] |= (uint32_t)(q0 & 0xFF) << (8 * (i & 3));
+        pk[1][i >> 2] |= (uint32_t)(q1 & 0xFF) << (8 * (i & 3));
+        pk[2][i >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (i & 3));
+        sum[0] += q0;
+        sum[1] += q1;
+        sum[2] += q2;
     }
 #pragma unroll
     for (int sp = 0; sp < 3; ++sp) {
-        const int col = 3 * m + sp;
-        uint2 packed;
-        packed.x = (uint32_t)(uint8_t)q[sp][0] | ((uint32_t)(uint8_t)q[sp][1] << 8) |
-                   ((uint32_t)(uint8_t)q[sp][2] << 16) | ((uint32_t)(uint8_t)q[sp][3] << 24);
-        packed.y = (uint32_t)(uint8_t)q[sp][4] | ((uint32_t)(uint8_t)q[sp][5] << 8) |
-                   ((uint32_t)(uint8_t)q[sp][6] << 16) | ((uint32_t)(uint8_t)q[sp][7] << 24);
-        *reinterpret_cast<uint2*>(p.xq + (int64_t)col * p.kx + k0) = packed;
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s += q[sp][i];
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        if ((lane & 1) == 0) p.s16[(int64_t)col * (p.kx / 16) + b * 16 + (lane >> 1)] = s;
+        const int c = 3 * m + sp;
+        *reinterpret_cast<uint2*>(p.xq + (int64_t)c * p.kx + k0) = make_uint2(pk[sp][0], pk[sp][1]);
+        int s = sum[sp] + __shfl_xor_sync(0xffffffffu, sum[sp], 1);
+        if ((lane & 1) == 0) p.s16[(int64_t)c * (p.kx / 16) + b * 16 + (lane >> 1)] = s;
         s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if ((lane & 3) == 0) p.s32[(int64_t)col * (p.kx / 32) + b * 8 + (lane >> 2)] = s;
+        if ((lane & 3) == 0) p.s32[(int64_t)c * (p.kx / 32) + b * 8 + (lane >> 2)] = s;
     }
     if (lane == 0)
         p.xs[(int64_t)m * (p.kx / 256) + b] =
             finite ? __uint_as_float((uint32_t)(127 + e) << 23) : __uint_as_float(0x7fc00000u);
 }
 
-// ---------------------------------------------------------------------------
-// Shared epilogue: reduce the per-warp partials in a fixed order and fold the
-// three int8 planes of each activation row.
-// ---------------------------------------------------------------------------
+// Shared-memory view of the activation planes of one CTA's K range.
+struct XSmem {
+    int8_t* q;   // [ncp][qstride]  plane c = 3m + s, natural k order
+    int32_t* s;  // [ncp][sstride]  per-32 (Q4_K) / per-16 (Q6_K) sums of each plane
+    float* xs;   // [mpad][umax]    block scales 2^e
+    int qstride, sstride, umax;
+};
+
+// ---- per-unit consumers, general layout (rows >= 2) ---------------------------
+// Columns 3m+s of the n8 tiles hold plane s of activation row m; lane (g, t)
+// owns rows g, g+8 x columns 2t, 2t+1 of each tile.
 template <int NT>
-__device__ __forceinline__ void epilogue(float (&acc)[NT][4], float* red, int ks, int rows, int64_t n,
-                                         int64_t rt, const float* __restrict__ bias, float* __restrict__ y) {
-    constexpr int C = NT * 8;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+__device__ __forceinline__ void consume_q4k(const uint8_t* rec, int l, const XSmem& X, float (&acc)[NT][4], int g,
+                                            int t, int lane) {
+    const uint4 h0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
+    uint4 q[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) q[c] = *reinterpret_cast<const uint4*>(rec + 256 + 512 * c + 16 * lane);
+    // 6-bit scales / mins, byte j of each word (rows g: *0, g+8: *1)
+    const uint32_t sc0[2] = {h0.y & 0x3F3F3F3Fu, (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u)};
+    const uint32_t mn0[2] = {h0.z & 0x3F3F3F3Fu, ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u)};
+    const uint32_t sc1[2] = {h1.y & 0x3F3F3F3Fu, (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)};
+    const uint32_t mn1[2] = {h1.z & 0x3F3F3F3Fu, ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u)};
+    const float d0 = h2f(h0.x & 0xffffu) * 0.0625f, dm0 = h2f(h0.x >> 16);
+    const float d1 = h2f(h1.x & 0xffffu) * 0.0625f, dm1 = h2f(h1.x >> 16);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        float* r0 = red + (warp * 16 + g) * C + nt * 8 + 2 * t;
-        float* r1 = red + (warp * 16 + g + 8) * C + nt * 8 + 2 * t;
-        r0[0] = acc[nt][0];
-        r0[1] = acc[nt][1];
-        r1[0] = acc[nt][2];
-        r1[1] = acc[nt][3];
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < 16 * rows; idx += blockDim.x) {
-        const int row = idx & 15, m = idx >> 4;
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f;
-        for (int w = 0; w < ks; ++w) {
-            const float* r = red + (w * 16 + row) * C + 3 * m;
-            p0 += r[0];
-            p1 += r[1];
-            p2 += r[2];
+        const int8_t* xb = X.q + (nt * 8 + g) * X.qstride + l * 256 + 8 * t;
+        int L0 = 0, L1 = 0, L2 = 0, L3 = 0, H0 = 0, H1 = 0, H2 = 0, H3 = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint2 bl = *reinterpret_cast<const uint2*>(xb + 64 * c);
+            const uint2 bh = *reinterpret_cast<const uint2*>(xb + 64 * c + 32);
+            int r[4], u[4];
+            mma_s8_k32(r, q[c].x & 0x0F0F0F0Fu, q[c].z & 0x0F0F0F0Fu, q[c].y & 0x0F0F0F0Fu, q[c].w & 0x0F0F0F0Fu,
+                       bl.x, bl.y);
+            // high nibbles in place: u8 values 16*q
+            mma_u8_k32(u, q[c].x & 0xF0F0F0F0u, q[c].z & 0xF0F0F0F0u, q[c].y & 0xF0F0F0F0u, q[c].w & 0xF0F0F0F0u,
+                       bh.x, bh.y);
+            const int j0 = 2 * c, j1 = 2 * c + 1;
+            const int s0l = zext_byte(sc0[j0 >> 2], j0 & 3), s0h = zext_byte(sc0[j1 >> 2], j1 & 3);
+            const int s1l = zext_byte(sc1[j0 >> 2], j0 & 3), s1h = zext_byte(sc1[j1 >> 2], j1 & 3);
+            L0 += s0l * r[0];
+            L1 += s0l * r[1];
+            L2 += s1l * r[2];
+            L3 += s1l * r[3];
+            H0 += s0h * u[0];
+            H1 += s0h * u[1];
+            H2 += s1h * u[2];
+            H3 += s1h * u[3];
         }
-        const int64_t o = rt * 16 + row;
-        if (o < n) {
-            float v = (p2 * (1.0f / 16384.0f) + p1 * (1.0f / 128.0f)) + p0;
-            if (bias) v += bias[o];
-            y[(int64_t)m * n + o] = v;
+        const int ca = nt * 8 + 2 * t, cb = ca + 1;
+        const int4* sa = reinterpret_cast<const int4*>(X.s + ca * X.sstride + l * 8);
+        const int4* sb = reinterpret_cast<const int4*>(X.s + cb * X.sstride + l * 8);
+        const int4 sa0 = sa[0], sa1 = sa[1], sb0 = sb[0], sb1 = sb[1];
+        const int Sa[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
+        const int Sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
+        int M0 = 0, M1 = 0, M2 = 0, M3 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int m0 = zext_byte(mn0[j >> 2], j & 3), m1 = zext_byte(mn1[j >> 2], j & 3);
+            M0 += m0 * Sa[j];
+            M1 += m0 * Sb[j];
+            M2 += m1 * Sa[j];
+            M3 += m1 * Sb[j];
         }
+        const float xa = X.xs[(ca / 3) * X.umax + l], xb2 = X.xs[(cb / 3) * X.umax + l];
+        acc[nt][0] += xa * (d0 * (float)(16 * L0 + H0) - dm0 * (float)M0);
+        acc[nt][1] += xb2 * (d0 * (float)(16 * L1 + H1) - dm0 * (float)M1);
+        acc[nt][2] += xa * (d1 * (float)(16 * L2 + H2) - dm1 * (float)M2);
+        acc[nt][3] += xb2 * (d1 * (float)(16 * L3 + H3) - dm1 * (float)M3);
     }
 }
 
-// ---------------------------------------------------------------------------
-// Q4_K
-// ---------------------------------------------------------------------------
-template <int NT>
-__global__ void __launch_bounds__(256) gemv_q4k_kernel(const uint8_t* __restrict__ W, int64_t n, int nkb, int ks,
-                                                       XPlanes p, int rows, const float* __restrict__ bias,
-                                                       float* __restrict__ y) {
-    extern __shared__ float red[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t rt = blockIdx.x;
-    const int kb0 = (int)((int64_t)nkb * warp / ks), kb1 = (int)((int64_t)nkb * (warp + 1) / ks);
-    const uint8_t* recs = W + (size_t)rt * nkb * 2304;
-    const int kx32 = p.kx / 32;
-
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) acc[nt][v] = 0.f;
-
-    uint4 h0, h1, q[4];
-    if (kb0 < kb1) {
-        const uint8_t* rec = recs + (size_t)kb0 * 2304;
-        h0 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * g));
-        h1 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * (g + 8)));
-#pragma unroll
-        for (int c = 0; c < 4; ++c) q[c] = ld_stream(rec + 256 + 512 * c + 16 * lane);
+// A operands of Q6_K sub-block j from the low-nibble word w and crumb word h.
+__device__ __forceinline__ void q6_frag(int j, uint32_t w, uint32_t h, uint32_t& a0, uint32_t& a1) {
+    if ((j & 1) == 0) {
+        a0 = (w & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);
+        a1 = ((w >> 4) & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);
+    } else {
+        a0 = (w & 0x0F0F0F0Fu) | (h & 0x30303030u);
+        a1 = ((w >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u);
     }
-    for (int kb = kb0; kb < kb1; ++kb) {
-        uint4 nh0 = h0, nh1 = h1, nq[4] = {q[0], q[1], q[2], q[3]};
-        if (kb + 1 < kb1) {
-            const uint8_t* rec = recs + (size_t)(kb + 1) * 2304;
-            nh0 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * g));
-            nh1 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * (g + 8)));
-#pragma unroll
-            for (int c = 0; c < 4; ++c) nq[c] = ld_stream(rec + 256 + 512 * c + 16 * lane);
-        }
-        // scales / mins of rows g (h0) and g+8 (h1)
-        int sc0[8], mn0[8], sc1[8], mn1[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            sc0[j] = (h0.y >> (8 * j)) & 63;
-            mn0[j] = (h0.z >> (8 * j)) & 63;
-            sc0[j + 4] = ((h0.w >> (8 * j)) & 0xF) | (((h0.y >> (8 * j + 6)) & 3) << 4);
-            mn0[j + 4] = ((h0.w >> (8 * j + 4)) & 0xF) | (((h0.z >> (8 * j + 6)) & 3) << 4);
-            sc1[j] = (h1.y >> (8 * j)) & 63;
-            mn1[j] = (h1.z >> (8 * j)) & 63;
-            sc1[j + 4] = ((h1.w >> (8 * j)) & 0xF) | (((h1.y >> (8 * j + 6)) & 3) << 4);
-            mn1[j + 4] = ((h1.w >> (8 * j + 4)) & 0xF) | (((h1.z >> (8 * j + 6)) & 3) << 4);
-        }
-        const float d0 = f16_bits_to_f32(h0.x & 0xffffu), dm0 = f16_bits_to_f32(h0.x >> 16);
-        const float d1 = f16_bits_to_f32(h1.x & 0xffffu), dm1 = f16_bits_to_f32(h1.x >> 16);
-
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int colb = nt * 8 + g;  // B column this lane supplies
-            const int8_t* xb = p.xq + (int64_t)colb * p.kx + (int64_t)kb * 256 + 8 * t;
-            int C[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const int j = 2 * c + half, sh = 4 * half;
-                    const uint2 bb = __ldg(reinterpret_cast<const uint2*>(xb + 32 * j));
-                    int r[4];
-                    mma_k32(r, (q[c].x >> sh) & 0x0F0F0F0Fu, (q[c].z >> sh) & 0x0F0F0F0Fu,
-                            (q[c].y >> sh) & 0x0F0F0F0Fu, (q[c].w >> sh) & 0x0F0F0F0Fu, bb.x, bb.y);
-                    C[0] += sc0[j] * r[0];
-                    C[1] += sc0[j] * r[1];
-                    C[2] += sc1[j] * r[2];
-                    C[3] += sc1[j] * r[3];
-                }
-            }
-            // min term with the exact per-32 sums of the two columns this lane owns
-            const int ca = nt * 8 + 2 * t, cb = ca + 1;
-            const int4* sa = reinterpret_cast<const int4*>(p.s32 + (int64_t)ca * kx32 + (int64_t)kb * 8);
-            const int4* sb = reinterpret_cast<const int4*>(p.s32 + (int64_t)cb * kx32 + (int64_t)kb * 8);
-            const int4 sa0 = __ldg(sa), sa1 = __ldg(sa + 1), sb0 = __ldg(sb), sb1 = __ldg(sb + 1);
-            const int Sa[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
-            const int Sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
-            int M0 = 0, M1 = 0, M2 = 0, M3 = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                M0 += mn0[j] * Sa[j];
-                M1 += mn0[j] * Sb[j];
-                M2 += mn1[j] * Sa[j];
-                M3 += mn1[j] * Sb[j];
-            }
-            const float xa = __ldg(p.xs + (int64_t)(ca / 3) * (p.kx / 256) + kb);
-            const float xb2 = __ldg(p.xs + (int64_t)(cb / 3) * (p.kx / 256) + kb);
-            acc[nt][0] += xa * (d0 * (float)C[0] - dm0 * (float)M0);
-            acc[nt][1] += xb2 * (d0 * (float)C[1] - dm0 * (float)M1);
-            acc[nt][2] += xa * (d1 * (float)C[2] - dm1 * (float)M2);
-            acc[nt][3] += xb2 * (d1 * (float)C[3] - dm1 * (float)M3);
-        }
-        h0 = nh0;
-        h1 = nh1;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) q[c] = nq[c];
-    }
-    epilogue<NT>(acc, red, ks, rows, n, rt, bias, y);
 }
 
-// ---------------------------------------------------------------------------
-// Q6_K
-// ---------------------------------------------------------------------------
 template <int NT>
-__global__ void __launch_bounds__(256) gemv_q6k_kernel(const uint8_t* __restrict__ W, int64_t n, int nkb, int ks,
-                                                       XPlanes p, int rows, const float* __restrict__ bias,
-                                                       float* __restrict__ y) {
-    extern __shared__ float red[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t rt = blockIdx.x;
-    const int kb0 = (int)((int64_t)nkb * warp / ks), kb1 = (int)((int64_t)nkb * (warp + 1) / ks);
-    const uint8_t* recs = W + (size_t)rt * nkb * 3360;
-    const int kx16 = p.kx / 16;
-
-    float acc[NT][4];
+__device__ __forceinline__ void consume_q6k(const uint8_t* rec, int l, const XSmem& X, float (&acc)[NT][4], int g,
+                                            int t, int lane) {
+    const uint4 s0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
+    const uint4 s1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
+    const float d0 = h2f(*reinterpret_cast<const unsigned short*>(rec + 256 + 2 * g));
+    const float d1 = h2f(*reinterpret_cast<const unsigned short*>(rec + 256 + 2 * (g + 8)));
+    uint4 lo[4], hi[2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int u = 0; u < 4; ++u) lo[u] = *reinterpret_cast<const uint4*>(rec + 288 + 512 * u + 16 * lane);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) acc[nt][v] = 0.f;
-
-    uint4 s0, s1, lo[4], hi[2];
-    uint32_t dd0 = 0, dd1 = 0;
-    auto load = [&](int kb, uint4& a0, uint4& a1, uint32_t& e0, uint32_t& e1, uint4 (&l)[4], uint4 (&h)[2]) {
-        const uint8_t* rec = recs + (size_t)kb * 3360;
-        a0 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * g));
-        a1 = __ldg(reinterpret_cast<const uint4*>(rec + 16 * (g + 8)));
-        e0 = __ldg(reinterpret_cast<const unsigned short*>(rec + 256 + 2 * g));
-        e1 = __ldg(reinterpret_cast<const unsigned short*>(rec + 256 + 2 * (g + 8)));
+    for (int v = 0; v < 2; ++v) hi[v] = *reinterpret_cast<const uint4*>(rec + 2336 + 512 * v + 16 * lane);
+    const uint32_t sw0[4] = {s0.x, s0.y, s0.z, s0.w};
+    const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w};
+    const uint32_t lw[16] = {lo[0].x, lo[0].y, lo[0].z, lo[0].w, lo[1].x, lo[1].y, lo[1].z, lo[1].w,
+                             lo[2].x, lo[2].y, lo[2].z, lo[2].w, lo[3].x, lo[3].y, lo[3].z, lo[3].w};
+    const uint32_t hw[8] = {hi[0].x, hi[0].y, hi[0].z, hi[0].w, hi[1].x, hi[1].y, hi[1].z, hi[1].w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) l[u] = ld_stream(rec + 288 + 512 * u + 16 * lane);
+    for (int nt = 0; nt < NT; ++nt) {
+        const int8_t* xb = X.q + (nt * 8 + g) * X.qstride + l * 256 + 4 * t;
+        const int ca = nt * 8 + 2 * t, cb = ca + 1;
+        const int4* sa = reinterpret_cast<const int4*>(X.s + ca * X.sstride + l * 16);
+        const int4* sb = reinterpret_cast<const int4*>(X.s + cb * X.sstride + l * 16);
+        int C[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int v = 0; v < 2; ++v) h[v] = ld_stream(rec + 2336 + 512 * v + 16 * lane);
-    };
-    if (kb0 < kb1) load(kb0, s0, s1, dd0, dd1, lo, hi);
-    for (int kb = kb0; kb < kb1; ++kb) {
-        uint4 ns0 = s0, ns1 = s1, nlo[4] = {lo[0], lo[1], lo[2], lo[3]}, nhi[2] = {hi[0], hi[1]};
-        uint32_t nd0 = dd0, nd1 = dd1;
-        if (kb + 1 < kb1) load(kb + 1, ns0, ns1, nd0, nd1, nlo, nhi);
-
-        const uint32_t sw0[4] = {s0.x, s0.y, s0.z, s0.w};
-        const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w};
-        const uint32_t lw[16] = {lo[0].x, lo[0].y, lo[0].z, lo[0].w, lo[1].x, lo[1].y, lo[1].z, lo[1].w,
-                                 lo[2].x, lo[2].y, lo[2].z, lo[2].w, lo[3].x, lo[3].y, lo[3].z, lo[3].w};
-        const uint32_t hw[8] = {hi[0].x, hi[0].y, hi[0].z, hi[0].w, hi[1].x, hi[1].y, hi[1].z, hi[1].w};
-        const float d0 = f16_bits_to_f32(dd0), d1 = f16_bits_to_f32(dd1);
-
+        for (int j4 = 0; j4 < 4; ++j4) {
+            const int4 A = sa[j4], B = sb[j4];
+            const int SA[4] = {A.x, A.y, A.z, A.w}, SB[4] = {B.x, B.y, B.z, B.w};
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int colb = nt * 8 + g;
-            const int8_t* xb = p.xq + (int64_t)colb * p.kx + (int64_t)kb * 256 + 4 * t;
-            const int ca = nt * 8 + 2 * t, cb = ca + 1;
-            const int4* sa = reinterpret_cast<const int4*>(p.s16 + (int64_t)ca * kx16 + (int64_t)kb * 16);
-            const int4* sb = reinterpret_cast<const int4*>(p.s16 + (int64_t)cb * kx16 + (int64_t)kb * 16);
-            int C[4] = {0, 0, 0, 0}, Mn[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                const int4 A = __ldg(sa + j4), B = __ldg(sb + j4);
-                const int SA[4] = {A.x, A.y, A.z, A.w}, SB[4] = {B.x, B.y, B.z, B.w};
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    const int j = 4 * j4 + jj;
-                    const uint32_t w = lw[j], h = hw[j >> 1];
-                    uint32_t a0, a1;
-                    if ((j & 1) == 0) {
-                        a0 = (w & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);
-                        a1 = ((w >> 4) & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);
-                    } else {
-                        a0 = (w & 0x0F0F0F0Fu) | (h & 0x30303030u);
-                        a1 = ((w >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u);
-                    }
-                    const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t*>(xb + 16 * j));
-                    int r[4];
-                    mma_k16(r, a0, a1, b0);
-                    const int scg = (int)(int8_t)(sw0[j >> 2] >> (8 * (j & 3)));
-                    const int sch = (int)(int8_t)(sw1[j >> 2] >> (8 * (j & 3)));
-                    C[0] += scg * r[0];
-                    C[1] += scg * r[1];
-                    C[2] += sch * r[2];
-                    C[3] += sch * r[3];
-                    Mn[0] += scg * SA[jj];
-                    Mn[1] += scg * SB[jj];
-                    Mn[2] += sch * SA[jj];
-                    Mn[3] += sch * SB[jj];
-                }
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = 4 * j4 + jj;
+                uint32_t a0, a1;
+                q6_frag(j, lw[j], hw[j >> 1], a0, a1);
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
+                int r[4];
+                mma_s8_k16(r, a0, a1, b0);
+                const int scg = sext_byte(sw0[j >> 2], j & 3), sch = sext_byte(sw1[j >> 2], j & 3);
+                C[0] += scg * (r[0] - 32 * SA[jj]);
+                C[1] += scg * (r[1] - 32 * SB[jj]);
+                C[2] += sch * (r[2] - 32 * SA[jj]);
+                C[3] += sch * (r[3] - 32 * SB[jj]);
             }
-            const float xa = __ldg(p.xs + (int64_t)(ca / 3) * (p.kx / 256) + kb);
-            const float xb2 = __ldg(p.xs + (int64_t)(cb / 3) * (p.kx / 256) + kb);
-            acc[nt][0] += xa * (d0 * (float)(C[0] - 32 * Mn[0]));
-            acc[nt][1] += xb2 * (d0 * (float)(C[1] - 32 * Mn[1]));
-            acc[nt][2] += xa * (d1 * (float)(C[2] - 32 * Mn[2]));
-            acc[nt][3] += xb2 * (d1 * (float)(C[3] - 32 * Mn[3]));
         }
-        s0 = ns0;
-        s1 = ns1;
-        dd0 = nd0;
-        dd1 = nd1;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) lo[u] = nlo[u];
-        hi[0] = nhi[0];
-        hi[1] = nhi[1];
+        const float xa = X.xs[(ca / 3) * X.umax + l], xb2 = X.xs[(cb / 3) * X.umax + l];
+        acc[nt][0] += xa * (d0 * (float)C[0]);
+        acc[nt][1] += xb2 * (d0 * (float)C[1]);
+        acc[nt][2] += xa * (d1 * (float)C[2]);
+        acc[nt][3] += xb2 * (d1 * (float)C[3]);
     }
-    epilogue<NT>(acc, red, ks, rows, n, rt, bias, y);
 }
 
-// ---------------------------------------------------------------------------
-// Q8_0 (records of 16 rows x 32 k; a warp step covers 8 records = 256 k)
-// ---------------------------------------------------------------------------
+// Q8_0 unit = up to 8 consecutive 544-byte records (16 rows x 32 k each).
 template <int NT>
-__global__ void __launch_bounds__(256) gemv_q80_kernel(const uint8_t* __restrict__ W, int64_t n, int nkb, int ks,
-                                                       XPlanes p, int rows, const float* __restrict__ bias,
-                                                       float* __restrict__ y) {
-    extern __shared__ float red[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t rt = blockIdx.x;
-    const int ngrp = (nkb + 7) / 8;
-    const int gr0 = (int)((int64_t)ngrp * warp / ks), gr1 = (int)((int64_t)ngrp * (warp + 1) / ks);
-    const uint8_t* recs = W + (size_t)rt * nkb * 544;
-
-    float acc[NT][4];
+__device__ __forceinline__ void consume_q80(const uint8_t* rec, int l, int nb, const XSmem& X, float (&acc)[NT][4],
+                                            int g, int t, int lane) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) acc[nt][v] = 0.f;
-
-    for (int gr = gr0; gr < gr1; ++gr) {
-        const int b0 = gr * 8, nb = min(8, nkb - b0);
-        uint4 q[8];
-        uint32_t e0[8], e1[8];
+    for (int nt = 0; nt < NT; ++nt) {
+        const int8_t* xb = X.q + (nt * 8 + g) * X.qstride + l * 256 + 4 * t;
+        float blk[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (i < nb) {
-                const uint8_t* rec = recs + (size_t)(b0 + i) * 544;
-                q[i] = ld_stream(rec + 32 + 16 * lane);
-                e0[i] = __ldg(reinterpret_cast<const unsigned short*>(rec + 2 * g));
-                e1[i] = __ldg(reinterpret_cast<const unsigned short*>(rec + 2 * (g + 8)));
-            } else {
-                q[i] = make_uint4(0, 0, 0, 0);
-                e0[i] = e1[i] = 0;
+                const uint8_t* r8 = rec + 544 * i;
+                const uint4 q = *reinterpret_cast<const uint4*>(r8 + 32 + 16 * lane);
+                const float dg = h2f(*reinterpret_cast<const unsigned short*>(r8 + 2 * g));
+                const float dh = h2f(*reinterpret_cast<const unsigned short*>(r8 + 2 * (g + 8)));
+                const uint32_t bx = *reinterpret_cast<const uint32_t*>(xb + 32 * i);
+                const uint32_t by = *reinterpret_cast<const uint32_t*>(xb + 32 * i + 16);
+                int r[4];
+                mma_s8_k32(r, q.x, q.y, q.z, q.w, bx, by);
+                blk[0] += dg * (float)r[0];
+                blk[1] += dg * (float)r[1];
+                blk[2] += dh * (float)r[2];
+                blk[3] += dh * (float)r[3];
             }
         }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int colb = nt * 8 + g;
-            const int ca = nt * 8 + 2 * t, cb = ca + 1;
-            const float xa = __ldg(p.xs + (int64_t)(ca / 3) * (p.kx / 256) + gr);
-            const float xb2 = __ldg(p.xs + (int64_t)(cb / 3) * (p.kx / 256) + gr);
-            float blk[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (i < nb) {
-                    const int8_t* xb = p.xq + (int64_t)colb * p.kx + (int64_t)(b0 + i) * 32 + 4 * t;
-                    const uint32_t bx = __ldg(reinterpret_cast<const uint32_t*>(xb));
-                    const uint32_t by = __ldg(reinterpret_cast<const uint32_t*>(xb + 16));
-                    int r[4];
-                    mma_k32(r, q[i].x, q[i].y, q[i].z, q[i].w, bx, by);
-                    const float dg = f16_bits_to_f32(e0[i]), dh = f16_bits_to_f32(e1[i]);
-                    blk[0] += dg * (float)r[0];
-                    blk[1] += dg * (float)r[1];
-                    blk[2] += dh * (float)r[2];
-                    blk[3] += dh * (float)r[3];
-                }
-            }
-            acc[nt][0] += xa * blk[0];
-            acc[nt][1] += xb2 * blk[1];
-            acc[nt][2] += xa * blk[2];
-            acc[nt][3] += xb2 * blk[3];
-        }
+        const int ca = nt * 8 + 2 * t, cb = ca + 1;
+        const float xa = X.xs[(ca / 3) * X.umax + l], xb2 = X.xs[(cb / 3) * X.umax + l];
+        acc[nt][0] += xa * blk[0];
+        acc[nt][1] += xb2 * blk[1];
+        acc[nt][2] += xa * blk[2];
+        acc[nt][3] += xb2 * blk[3];
     }
-    epilogue<NT>(acc, red, ks, rows, n, rt, bias, y);
 }
 
-template <int NT>
-cudaError_t launch_nt(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
-                      const float* bias, float* y, int sms, cudaStream_t s) {
-    const int64_t n_rt = (n + 15) / 16;
-    const int units = type == kQ8_0 ? (int)((k / 32 + 7) / 8) : (int)(k / 256);
-    // enough warps to keep ~16 per SM streaming, at most 8 per CTA
-    int64_t ks = (int64_t)sms * 16 / n_rt;
-    if (ks < 1) ks = 1;
-    if (ks > 8) ks = 8;
-    if (ks > units) ks = units;
-    const size_t smem = (size_t)ks * 16 * NT * 8 * sizeof(float);
-    const dim3 grid((unsigned)n_rt), block((unsigned)(32 * ks));
-    const uint8_t* w = (const uint8_t*)tiles;
-    if (type == kQ4_K)
-        gemv_q4k_kernel<NT><<<grid, block, smem, s>>>(w, n, (int)(k / 256), (int)ks, p, rows, bias, y);
-    else if (type == kQ6_K)
-        gemv_q6k_kernel<NT><<<grid, block, smem, s>>>(w, n, (int)(k / 256), (int)ks, p, rows, bias, y);
-    else
-        gemv_q80_kernel<NT><<<grid, block, smem, s>>>(w, n, (int)(k / 32), (int)ks, p, rows, bias, y);
-    return cudaGetLastError();
+// ---- single activation row (M = 1) -----------------------------------------
+// The three planes sit in MMA columns 0, 2 and 4 (lane t's even column 2t holds
+// plane t for t < 3); odd columns and column 6 read a zero row.  Each lane then
+// keeps only its two useful accumulators (rows g and g+8, plane t).
+__device__ __forceinline__ int m1_bplane(int g) { return ((g & 1) == 0 && g < 6) ? (g >> 1) : 3; }
+
+__device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const XSmem& X, float& acc0,
+                                               float& acc2, int g, int t, int lane) {
+    const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 8 * t;
+    const uint4 h0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
+    uint4 q[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) q[c] = *reinterpret_cast<const uint4*>(rec + 256 + 512 * c + 16 * lane);
+    const uint32_t sc0[2] = {h0.y & 0x3F3F3F3Fu, (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u)};
+    const uint32_t mn0[2] = {h0.z & 0x3F3F3F3Fu, ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u)};
+    const uint32_t sc1[2] = {h1.y & 0x3F3F3F3Fu, (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)};
+    const uint32_t mn1[2] = {h1.z & 0x3F3F3F3Fu, ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u)};
+    int lo0 = 0, hi0 = 0, lo2 = 0, hi2 = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint2 bl = *reinterpret_cast<const uint2*>(xb + 64 * c);
+        const uint2 bh = *reinterpret_cast<const uint2*>(xb + 64 * c + 32);
+        int r[4], u[4];
+        mma_s8_k32(r, q[c].x & 0x0F0F0F0Fu, q[c].z & 0x0F0F0F0Fu, q[c].y & 0x0F0F0F0Fu, q[c].w & 0x0F0F0F0Fu, bl.x,
+                   bl.y);
+        mma_u8_k32(u, q[c].x & 0xF0F0F0F0u, q[c].z & 0xF0F0F0F0u, q[c].y & 0xF0F0F0F0u, q[c].w & 0xF0F0F0F0u, bh.x,
+                   bh.y);
+        const int j0 = 2 * c, j1 = 2 * c + 1;
+        lo0 += zext_byte(sc0[j0 >> 2], j0 & 3) * r[0];
+        hi0 += zext_byte(sc0[j1 >> 2], j1 & 3) * u[0];
+        lo2 += zext_byte(sc1[j0 >> 2], j0 & 3) * r[2];
+        hi2 += zext_byte(sc1[j1 >> 2], j1 & 3) * u[2];
+    }
+    const int4* sp = reinterpret_cast<const int4*>(X.s + (t < 3 ? t : 3) * X.sstride + l * 8);
+    const int4 sa0 = sp[0], sa1 = sp[1];
+    const int S[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
+    int M0 = 0, M2 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        M0 += zext_byte(mn0[j >> 2], j & 3) * S[j];
+        M2 += zext_byte(mn1[j >> 2], j & 3) * S[j];
+    }
+    const float xs = X.xs[l];
+    const float d0 = h2f(h0.x & 0xffffu) * 0.0625f, dm0 = h2f(h0.x >> 16);
+    const float d1 = h2f(h1.x & 0xffffu) * 0.0625f, dm1 = h2f(h1.x >> 16);
+    acc0 += xs * (d0 * (float)(16 * lo0 + hi0) - dm0 * (float)M0);
+    acc2 += xs * (d1 * (float)(16 * lo2 + hi2) - dm1 * (float)M2);
+}
+
+__device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const XSmem& X, float& acc0,
+                                               float& acc2, int g, int t, int lane) {
+    const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 4 * t;
+    const uint4 s0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
+    const uint4 s1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
+    uint4 lo[4], hi[2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) lo[u] = *reinterpret_cast<const uint4*>(rec + 288 + 512 * u + 16 * lane);
+#pragma unroll
+    for (int v = 0; v < 2; ++v) hi[v] = *reinterpret_cast<const uint4*>(rec + 2336 + 512 * v + 16 * lane);
+    const uint32_t sw0[4] = {s0.x, s0.y, s0.z, s0.w};
+    const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w};
+    const uint32_t lw[16] = {lo[0].x, lo[0].y, lo[0].z, lo[0].w, lo[1].x, lo[1].y, lo[1].z, lo[1].w,
+                             lo[2].x, lo[2].y, lo[2].z, lo[2].w, lo[3].x, lo[3].y, lo[3].z, lo[3].w};
+    const uint32_t hw[8] = {hi[0].x, hi[0].y, hi[0].z, hi[0].w, hi[1].x, hi[1].y, hi[1].z, hi[1].w};
+    const int4* sp = reinterpret_cast<const int4*>(X.s + (t < 3 ? t : 3) * X.sstride + l * 16);
+    int C0 = 0, C2 = 0;
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+        const int4 A = sp[j4];
+        const int SA[4] = {A.x, A.y, A.z, A.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = 4 * j4 + jj;
+            uint32_t a0, a1;
+            q6_frag(j, lw[j], hw[j >> 1], a0, a1);
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
+            int r[4];
+            mma_s8_k16(r, a0, a1, b0);
+            const int off = -32 * SA[jj];
+            C0 += sext_byte(sw0[j >> 2], j & 3) * (r[0] + off);
+            C2 += sext_byte(sw1[j >> 2], j & 3) * (r[2] + off);
+        }
+    }
+    const float xs = X.xs[l];
+    const float d0 = h2f(*reinterpret_cast<const unsigned short*>(rec + 256 + 2 * g));
+    const float d1 = h2f(*reinterpret_cast<const unsigned short*>(rec + 256 + 2 * (g + 8)));
+    acc0 += xs * (d0 * (float)C0);
+    acc2 += xs * (d1 * (float)C2);
+}
+
+__device__ __forceinline__ void consume_q80_m1(const uint8_t* rec, int l, int nb, const XSmem& X, float& acc0,
+                                               float& acc2, int g, int t, int lane) {
+    const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 4 * t;
+    float b0 = 0.f, b2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < nb) {
+            const uint8_t* r8 = rec + 544 * i;
+            const uint4 q = *reinterpret_cast<const uint4*>(r8 + 32 + 16 * lane);
+            const uint32_t bx = *reinterpret_cast<const uint32_t*>(xb + 32 * i);
+            const uint32_t by = *reinterpret_cast<const uint32_t*>(xb + 32 * i + 16);
+            int r[4];
+            mma_s8_k32(r, q.x, q.y, q.z, q.w, bx, by);
+            b0 += h2f(*reinterpret_cast<const unsigned short*>(r8 + 2 * g)) * (float)r[0];
+            b2 += h2f(*reinterpret_cast<const unsigned short*>(r8 + 2 * (g + 8))) * (float)r[2];
+        }
+    }
+    const float xs = X.xs[l];
+    acc0 += xs * b0;
+    acc2 += xs * b2;
+}
+
+// Shared-memory carve-up of one CTA (host and device agree on it).  nt == 0 is
+// the single-row layout: planes 0..2 plus a zero row for idle MMA columns.
+struct SmemMap {
+    int ring, bars, red, xq, xsum, xs, total;
+};
+__host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows) {
+    const int nc = nt * 8, mpad = nt ? (nc + 2) / 3 : 1, ncp = nt ? 3 * mpad : 4;
+    const int qstride = umax * 256 + 32;
+    const int sstride = sum_per(type) ? umax * sum_per(type) + 4 : 0;
+    SmemMap m;
+    m.ring = 0;
+    m.bars = kWarps * kStages * unit_bytes(type);
+    m.red = m.bars + (kWarps * kStages + 2) * 8;              // +1 barrier for the planes, padded
+    m.xq = (m.red + kWarps * 16 * rows * 4 + 127) & ~127;      // per-warp folded outputs
+    m.xsum = m.xq + ncp * qstride;
+    m.xs = m.xsum + ncp * sstride * 4;
+    m.total = m.xs + mpad * umax * 4;
+    return m;
+}
+
+// ---------------------------------------------------------------------------
+// The streaming kernel.  CTA = RT row tiles x KW warps per row tile (RT*KW = 8);
+// blockIdx.y = cross-CTA K split.  Warp w owns row tile (w % RT) and K slice
+// (w / RT) of the CTA's range.
+// ---------------------------------------------------------------------------
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+    // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
+    constexpr int UB = unit_bytes(TYPE), S = kStages, NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
+    constexpr int NCP = NT ? 3 * MPAD : 3;  // plane rows copied from global
+    constexpr int NTA = NT ? NT : 1;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int RT = a.rt_per_cta, KW = kWarps / RT;
+    const int split = blockIdx.y;
+    const int kw = warp / RT;
+    // CTA range [U0, U1); this warp's slice [u0, u1) inside it
+    const int U0 = (int)((int64_t)a.n_units * split / a.ks), U1 = (int)((int64_t)a.n_units * (split + 1) / a.ks);
+    const int u0 = U0 + (int)((int64_t)(U1 - U0) * kw / KW), u1 = U0 + (int)((int64_t)(U1 - U0) * (kw + 1) / KW);
+    const int nu = u1 - u0;
+    const int64_t rt = (int64_t)blockIdx.x * RT + (warp % RT);
+    const bool active = rt < a.n_rt;
+    const SmemMap map = smem_map(TYPE, NT, a.umax, a.rows);
+
+    uint8_t* ring = smem + map.ring + warp * (S * UB);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + map.bars) + warp * S;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + map.bars) + kWarps * S;
+    float* red = reinterpret_cast<float*>(smem + map.red);
+    const XSmem X{reinterpret_cast<int8_t*>(smem + map.xq), reinterpret_cast<int32_t*>(smem + map.xsum),
+                  reinterpret_cast<float*>(smem + map.xs), a.umax * 256 + 32,
+                  sum_per(TYPE) ? a.umax * sum_per(TYPE) + 4 : 0, a.umax};
+
+    auto unit_src = [&](int u, uint32_t& bytes) -> const uint8_t* {
+        if (TYPE == kQ8_0) {
+            const int b0 = 8 * u, nb = min(8, a.nblk - b0);
+            bytes = (uint32_t)(nb * 544);
+            return a.W + ((size_t)rt * a.nblk + b0) * 544;
+        }
+        bytes = UB;
+        return a.W + ((size_t)rt * a.n_units + u) * UB;
+    };
+
+    // 1. start the weight stream (weights do not depend on the previous kernel)
+    int issued = 0;
+    if (lane == 0) {
+        if (active)
+            for (int i = 0; i < S; ++i) mbar_init(&bars[i], 1);
+        if (warp == 0) mbar_init(xbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (active) {
+            for (; issued < S && issued < nu; ++issued) {
+                uint32_t bytes;
+                const uint8_t* src = unit_src(u0 + issued, bytes);
+                mbar_expect_tx(&bars[issued], bytes);
+                bulk_g2s(ring + issued * UB, src, bytes, &bars[issued]);
+            }
+        }
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    __syncthreads();  // barrier inits visible to every warp
+
+    // 2. activation planes of [U0, U1): wait for the split kernel, then copy
+    pdl_wait();
+    pdl_trigger();
+    const int NU = U1 - U0;
+    if (warp == 0) {
+        const uint32_t qb = (uint32_t)NU * 256, sb = (uint32_t)(NU * sum_per(TYPE) * 4);
+        if (lane == 0) mbar_expect_tx(xbar, NCP * (qb + sb));
+        __syncwarp();
+        for (int c = lane; c < NCP; c += 32) {
+            bulk_g2s(X.q + c * X.qstride, a.p.xq + (int64_t)c * a.p.kx + (int64_t)U0 * 256, qb, xbar);
+            if (sum_per(TYPE)) {
+                const int32_t* src = (TYPE == kQ4_K) ? a.p.s32 : a.p.s16;
+                const int64_t gstride = (int64_t)(a.p.kx / 256) * sum_per(TYPE);
+                bulk_g2s(X.s + c * X.sstride, src + (int64_t)c * gstride + (int64_t)U0 * sum_per(TYPE), sb, xbar);
+            }
+        }
+    }
+    for (int i = threadIdx.x; i < MPAD * NU; i += blockDim.x) {
+        const int m = i / NU, o = i - m * NU;
+        X.xs[m * X.umax + o] = a.p.xs[(int64_t)m * (a.p.kx / 256) + U0 + o];
+    }
+    if (NT == 0) {  // zero row read by idle MMA columns
+        for (int i = threadIdx.x; i < X.qstride / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(X.q + 3 * X.qstride)[i] = make_uint4(0, 0, 0, 0);
+        for (int i = threadIdx.x; i < X.sstride; i += blockDim.x) X.s[3 * X.sstride + i] = 0;
+    }
+    bool ok = mbar_wait_bounded(xbar, 0);
+    __syncthreads();
+
+    // 3. consume the ring (units are local to the CTA range: l = u - U0)
+    float acc[NTA][4];
+#pragma unroll
+    for (int nt = 0; nt < NTA; ++nt)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[nt][v] = 0.f;
+    int done = 0;
+    if (active) {
+        for (; done < nu && ok; ++done) {
+            const int st = done % S;
+            if (!mbar_wait_bounded(&bars[st], (uint32_t)((done / S) & 1))) {
+                ok = false;
+                break;
+            }
+            const uint8_t* rec = ring + st * UB;
+            const int l = u0 + done - U0;
+            if constexpr (NT == 0) {
+                if (TYPE == kQ4_K) consume_q4k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
+                else if (TYPE == kQ6_K) consume_q6k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
+                else consume_q80_m1(rec, l, min(8, a.nblk - 8 * (u0 + done)), X, acc[0][0], acc[0][2], g, t, lane);
+            } else {
+                if (TYPE == kQ4_K) consume_q4k<NT>(rec, l, X, acc, g, t, lane);
+                else if (TYPE == kQ6_K) consume_q6k<NT>(rec, l, X, acc, g, t, lane);
+                else consume_q80<NT>(rec, l, min(8, a.nblk - 8 * (u0 + done)), X, acc, g, t, lane);
+            }
+            __syncwarp();
+            if (lane == 0 && issued < nu) {
+                uint32_t bytes;
+                const uint8_t* src = unit_src(u0 + issued, bytes);
+                fence_proxy_async();
+                mbar_expect_tx(&bars[st], bytes);
+                bulk_g2s(ring + st * UB, src, bytes, &bars[st]);
+                ++issued;
+            }
+            issued = __shfl_sync(0xffffffffu, issued, 0);
+        }
+        if (!ok) {
+            // drain this warp's copies still in flight before its shared memory goes away
+            for (int i = done; i < issued; ++i) mbar_wait_bounded(&bars[i % S], (uint32_t)((i / S) & 1));
+            if (lane == 0) atomicAdd(a.err + 1, 1u);
+        }
+    }
+
+    // 4. fold the three planes of each activation row -> red[warp][m][row]
+    if constexpr (NT == 0) {
+        // lanes 4g+0,1,2 hold planes 0,1,2 of rows g and g+8
+        const float p1a = __shfl_sync(0xffffffffu, acc[0][0], 4 * g + 1);
+        const float p2a = __shfl_sync(0xffffffffu, acc[0][0], 4 * g + 2);
+        const float p1b = __shfl_sync(0xffffffffu, acc[0][2], 4 * g + 1);
+        const float p2b = __shfl_sync(0xffffffffu, acc[0][2], 4 * g + 2);
+        if (t == 0) {
+            red[warp * 16 + g] = (p2a * (1.0f / 16384.0f) + p1a * (1.0f / 128.0f)) + acc[0][0];
+            red[warp * 16 + g + 8] = (p2b * (1.0f / 16384.0f) + p1b * (1.0f / 128.0f)) + acc[0][2];
+        }
+    } else {
+        float* tmp = reinterpret_cast<float*>(ring);  // this warp's ring is drained
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < NTA; ++nt) {
+            tmp[g * NC + nt * 8 + 2 * t] = acc[nt][0];
+            tmp[g * NC + nt * 8 + 2 * t + 1] = acc[nt][1];
+            tmp[(g + 8) * NC + nt * 8 + 2 * t] = acc[nt][2];
+            tmp[(g + 8) * NC + nt * 8 + 2 * t + 1] = acc[nt][3];
+        }
+        __syncwarp();
+        for (int idx = lane; idx < 16 * a.rows; idx += 32) {
+            const int row = idx & 15, m = idx >> 4;
+            const float* r = tmp + row * NC + 3 * m;
+            red[(warp * a.rows + m) * 16 + row] = (r[2] * (1.0f / 16384.0f) + r[1] * (1.0f / 128.0f)) + r[0];
+        }
+    }
+    __syncthreads();
+
+    // 5. add the KW slices of each row tile in slice order; write y or a partial
+    const int64_t r0 = (int64_t)blockIdx.x * RT * 16;
+    for (int idx = threadIdx.x; idx < RT * 16 * a.rows; idx += blockDim.x) {
+        const int m = idx / (RT * 16), rl = idx - m * RT * 16;
+        const int tile = rl >> 4, row = rl & 15;
+        const int64_t o = r0 + rl;
+        if (o >= a.n) continue;
+        float v = 0.f;
+        for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
+        if (a.ks == 1) a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+        else a.part[((int64_t)split * a.rows + m) * a.n + o] = v;
+    }
+    if (a.ks == 1) return;
+
+    // 6. cross-CTA split: the last CTA of this row group adds in split order
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned int last;
+    if (threadIdx.x == 0) last = (atomicAdd(a.counters + blockIdx.x, 1u) == (unsigned)(a.ks - 1));
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int64_t nr = min((int64_t)RT * 16, a.n - r0);
+    for (int64_t idx = threadIdx.x; idx < nr * a.rows; idx += blockDim.x) {
+        const int m = (int)(idx / nr);
+        const int64_t o = r0 + (idx - (int64_t)m * nr);
+        float v = 0.f;
+        for (int s2 = 0; s2 < a.ks; ++s2) v += __ldcg(a.part + ((int64_t)s2 * a.rows + m) * a.n + o);
+        a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+    }
+    if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
+}
+
+template <int TYPE, int NT>
+cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
+    static size_t configured = 0;  // per template instance: largest dynamic smem enabled so far
+    if (pl.smem > 48 * 1024 && pl.smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)pl.smem);
+        if (e != cudaSuccess) return e;
+        configured = pl.smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)pl.groups, (unsigned)pl.ks);
+    cfg.blockDim = dim3(32 * kWarps);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT>, a);
+}
+
+template <int TYPE>
+cudaError_t launch_nt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
+    switch (pl.nt) {
+        case 0: return launch_typed<TYPE, 0>(pl, a, pdl, s);
+        case 1: return launch_typed<TYPE, 1>(pl, a, pdl, s);
+        case 2: return launch_typed<TYPE, 2>(pl, a, pdl, s);
+        case 3: return launch_typed<TYPE, 3>(pl, a, pdl, s);
+        case 4: return launch_typed<TYPE, 4>(pl, a, pdl, s);
+        case 5: return launch_typed<TYPE, 5>(pl, a, pdl, s);
+        case 6: return launch_typed<TYPE, 6>(pl, a, pdl, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace
+
+GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
+    GemvPlan pl{};
+    pl.nt = rows == 1 ? 0 : (3 * rows + 7) / 8;
+    pl.n_rt = (n + 15) / 16;
+    pl.n_units = (int)((k + 255) / 256);
+    // Aim for ~16 streaming warps per SM with at least two units per warp.  K is
+    // split first across the warps of a CTA (shared-memory reduction); the
+    // activation planes a CTA stages grow with rows, so wider activations keep
+    // 8 row tiles per CTA and split K across CTAs instead.
+    const int64_t want = (int64_t)16 * sms;
+    int64_t slices = (want + pl.n_rt - 1) / pl.n_rt;  // K slices per row tile
+    const int64_t max_slices = pl.n_units / 2 > 0 ? pl.n_units / 2 : 1;
+    if (slices > max_slices) slices = max_slices;
+    if (slices < 1) slices = 1;
+    int kw = 1;
+    if (rows <= 2)
+        while (kw * 2 <= kWarps && kw * 2 <= slices) kw *= 2;
+    int ks = (int)((slices + kw - 1) / kw);
+    auto fits = [&](int ks_) {
+        const int umax = (pl.n_units + ks_ - 1) / ks_;
+        return smem_map(type, pl.nt, umax, rows).total <= 220 * 1024;
+    };
+    while (!fits(ks) && ks < pl.n_units) ++ks;
+    if (const char* f = getenv("OCL_GEMV_KW")) {  // tuning overrides for experiments
+        const int v = atoi(f);
+        if (v == 1 || v == 2 || v == 4 || v == 8) kw = v;
+    }
+    if (const char* f = getenv("OCL_GEMV_KS")) {
+        const int v = atoi(f);
+        if (v >= 1 && v <= pl.n_units && fits(v)) ks = v;
+    }
+    pl.kw = kw;
+    pl.ks = ks;
+    pl.groups = (pl.n_rt + (kWarps / kw) - 1) / (kWarps / kw);
+    pl.umax = (pl.n_units + ks - 1) / ks;
+    pl.smem = (size_t)smem_map(type, pl.nt, pl.umax, rows).total;
+    pl.part_floats = pl.ks > 1 ? (size_t)pl.ks * rows * n : 0;
+    return pl;
+}
 
 XPlanes xplanes_carve(void* base, int64_t k) {
     XPlanes p;
@@ -462,24 +782,44 @@ XPlanes xplanes_carve(void* base, int64_t k) {
     return p;
 }
 
-cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, cudaStream_t s) {
-    const int nt = (3 * rows + 7) / 8;
-    const int mpad = (nt * 8 + 2) / 3;  // activation rows whose planes the GEMV reads
-    xsplit_kernel<<<dim3((unsigned)(p.kx / 256), (unsigned)mpad), 32, 0, s>>>(x, rows, k, p);
-    return cudaGetLastError();
+cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s) {
+    const int nt = rows == 1 ? 0 : (3 * rows + 7) / 8;
+    const int mpad = nt ? (nt * 8 + 2) / 3 : 1;  // activation rows whose planes the GEMV reads
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.kx / 256), (unsigned)mpad);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, xsplit_kernel, x, rows, k, p);
 }
 
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
-                        const float* bias, float* y, int sms, cudaStream_t s) {
-    switch ((3 * rows + 7) / 8) {
-        case 1: return launch_nt<1>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        case 2: return launch_nt<2>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        case 3: return launch_nt<3>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        case 4: return launch_nt<4>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        case 5: return launch_nt<5>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        case 6: return launch_nt<6>(type, tiles, n, k, p, rows, bias, y, sms, s);
-        default: return cudaErrorInvalidValue;
-    }
+                        const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
+                        unsigned int* err, bool pdl, cudaStream_t s) {
+    GemvArgs a{};
+    a.W = (const uint8_t*)tiles;
+    a.n = n;
+    a.k = k;
+    a.n_rt = pl.n_rt;
+    a.n_units = pl.n_units;
+    a.nblk = (int)(k / 32);
+    a.ks = pl.ks;
+    a.rt_per_cta = kWarps / pl.kw;
+    a.umax = pl.umax;
+    a.p = p;
+    a.rows = rows;
+    a.bias = bias;
+    a.y = y;
+    a.part = part;
+    a.counters = counters;
+    a.err = err;
+    if (type == kQ4_K) return launch_nt<kQ4_K>(pl, a, pdl, s);
+    if (type == kQ6_K) return launch_nt<kQ6_K>(pl, a, pdl, s);
+    return launch_nt<kQ8_0>(pl, a, pdl, s);
 }
 
 }  // namespace ocl

@@ -42,10 +42,41 @@ cudaError_t launch_unpack(int type, const void* tiles, int64_t n_rows, int64_t k
 cudaError_t launch_embed(const void* tiles, int64_t n_rows, int64_t k, const int32_t* ids, int64_t n_ids,
                          float* out, unsigned int* bad, cudaStream_t s);
 
-// x [rows<=16, k] f32 -> planes.
-cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, cudaStream_t s);
-// y [rows<=16, n] = planes . W^T (+ bias).  `sms` = SM count of the device.
+// x [rows<=16, k] f32 -> planes (waits for the previous kernel when `pdl`).
+cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s);
+
+// Launch geometry of one GEMV.
+struct GemvPlan {
+    int nt;             // n8 tiles of activation planes (3*rows/8 rounded up); 0 = single-row layout
+    int64_t n_rt;       // 16-row tiles
+    int64_t groups;     // CTAs along N (8/kw row tiles each)
+    int kw;             // warps per row tile inside a CTA (K split in shared memory)
+    int n_units;        // 256-k units along K
+    int ks;             // K splits across CTAs
+    int umax;           // units in the largest CTA range
+    size_t smem;        // dynamic shared memory per CTA
+    size_t part_floats; // cross-CTA partial sums (0 when ks == 1)
+};
+GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms);
+
+struct GemvArgs {
+    const uint8_t* W;
+    int64_t n, k, n_rt;
+    int n_units, nblk, ks, rt_per_cta, umax;
+    XPlanes p;
+    int rows;
+    const float* bias;
+    float* y;
+    float* part;             // [ks][rows][n] when ks > 1
+    unsigned int* counters;  // [groups], zero between launches
+    unsigned int* err;       // [0] bad embedding ids, [1] bounded waits that gave up
+};
+
+// y [rows<=16, n] = planes . W^T (+ bias), geometry from plan_gemv.  `pdl`
+// launches with programmatic dependent launch (the kernel waits for its
+// predecessor before reading the planes).
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
-                        const float* bias, float* y, int sms, cudaStream_t s);
+                        const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
+                        unsigned int* err, bool pdl, cudaStream_t s);
 
 }  // namespace ocl
