@@ -73,7 +73,8 @@ typedef struct ocl_qbuf ocl_qbuf; /* a quantized weight resident in HBM */
 OCL_API int ocl_cuda_init(int device, ocl_ctx** out);
 OCL_API void ocl_cuda_destroy(ocl_ctx* ctx);
 /* Message of the last failing call on `ctx` ("" if none).  With ctx == NULL,
- * the message of the last failing ocl_cuda_init on this thread. */
+ * the message of the last failing context-free call (ocl_cuda_init,
+ * ocl_q_linear_noalloc) on this thread. */
 OCL_API const char* ocl_last_error(const ocl_ctx* ctx);
 /* Set the stream later calls launch on (NULL = legacy default stream). */
 OCL_API int ocl_set_stream(ocl_ctx* ctx, void* stream);
@@ -134,6 +135,28 @@ OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, si
 OCL_API int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size_t rows,
                       size_t in_features, size_t out_features, const float* bias_host,
                       float* y_host);
+
+/* Allocation-free variant of ocl_q_linear, for callers that cannot allocate
+ * GPU memory on the hot path: code running inside someone else's memory pool
+ * or under a strict no-allocation budget, plugins that may not call cudaMalloc
+ * (it can synchronise the device and stall the host), and hosts that must know
+ * their memory footprint up front.  No counterpart in the reference.
+ * It takes no context: `w_tiled_dev` is a weight already in OCL_LAYOUT_TILED16
+ * on the current device (e.g. ocl_q_device_ptr of an uploaded weight),
+ * x / bias / y are device pointers, and it launches on `stream` (cudaStream_t,
+ * NULL = default stream) on the current device.  Its scratch (activation planes,
+ * split-K partial sums and counters) is one static 4 MiB device array that
+ * every GPU loading this library holds until exit; in_features above 16384 or
+ * shapes whose partial sums exceed that array are rejected with
+ * OCL_ERR_UNSUPPORTED before any launch.  The first call on a device looks up
+ * that array's device address (no allocation); make the first call before any
+ * stream capture.  All calls share the array, so calls that overlap on the GPU
+ * (different streams or devices' contexts racing on one device) race on it:
+ * serialise them on one stream.  Results equal ocl_q_linear's.  Errors:
+ * ocl_last_error(NULL). */
+OCL_API int ocl_q_linear_noalloc(int ggml_type, const void* w_tiled_dev, size_t n_rows, size_t k,
+                                 const float* x_dev, size_t rows, const float* bias_dev, float* y_dev,
+                                 void* stream);
 
 /* Prefill: y bf16 [rows, out_features] = x bf16 [rows, in_features] . W^T, f32
  * accumulate on tcgen05 tensor cores (weights dequantized to bf16 tiles in

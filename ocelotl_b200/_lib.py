@@ -39,6 +39,7 @@ SIGNATURES = {
     "ocl_q_dequant": (C.c_int, [_vp, _vp, _vp]),
     "ocl_q_download_gguf": (C.c_int, [_vp, _vp, _vp]),
     "ocl_q_linear": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
+    "ocl_q_linear_noalloc": (C.c_int, [C.c_int, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
     "ocl_q_linear_host": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_gemm_bf16": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "ocl_q_embed_rows": (C.c_int, [_vp, _vp, _vp, _sz, _vp]),

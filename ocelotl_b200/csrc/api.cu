@@ -175,6 +175,11 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
 
 }  // namespace
 
+namespace ocl {
+// Message for ocl_last_error(NULL) from entry points that take no context.
+void set_thread_error(const char* msg) { g_init_err = msg; }
+}  // namespace ocl
+
 extern "C" {
 
 const char* ocl_backend_id(void) { return "cuda-sm100a"; }
