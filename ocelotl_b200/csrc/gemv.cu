@@ -44,7 +44,10 @@ namespace ocl {
 namespace {
 
 constexpr int kWarps = 8;   // warps per CTA
-constexpr int kStages = 2;  // ring depth per warp
+#ifndef OCL_GEMV_STAGES
+#define OCL_GEMV_STAGES 2
+#endif
+constexpr int kStages = OCL_GEMV_STAGES;  // ring depth per warp
 
 __host__ __device__ constexpr int unit_bytes(int t) { return t == kQ4_K ? 2304 : t == kQ6_K ? 3360 : 4352; }
 __host__ __device__ constexpr int sum_per(int t) { return t == kQ4_K ? 8 : t == kQ6_K ? 16 : 0; }
@@ -731,19 +734,18 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
     pl.nt = rows == 1 ? 0 : (3 * rows + 7) / 8;
     pl.n_rt = (n + 15) / 16;
     pl.n_units = (int)((k + 255) / 256);
-    // Aim for ~16 streaming warps per SM with at least two units per warp.  K is
-    // split first across the warps of a CTA (shared-memory reduction); the
-    // activation planes a CTA stages grow with rows, so wider activations keep
-    // 8 row tiles per CTA and split K across CTAs instead.
-    const int64_t want = (int64_t)16 * sms;
-    int64_t slices = (want + pl.n_rt - 1) / pl.n_rt;  // K slices per row tile
-    const int64_t max_slices = pl.n_units / 2 > 0 ? pl.n_units / 2 : 1;
-    if (slices > max_slices) slices = max_slices;
-    if (slices < 1) slices = 1;
+    // Measured on B200 (M = 1, Llama-shaped matrices): splitting K across
+    // CTAs never paid (its partial-sum round trip and fences cost more than the
+    // extra warps bring), and ~1500 streaming warps with K split 2-4 ways inside
+    // each CTA did best.  So: ks = 1 unless the staged activation planes do not
+    // fit in shared memory, and kw = the power of two nearest 1536 / row tiles
+    // (scaled by the SM count), capped at 4 and at half the K units.
     int kw = 1;
-    if (rows <= 2)
-        while (kw * 2 <= kWarps && kw * 2 <= slices) kw *= 2;
-    int ks = (int)((slices + kw - 1) / kw);
+    if (rows <= 2) {
+        const double target = 1536.0 * sms / 148.0 / (double)pl.n_rt;
+        while (kw < 4 && kw * 2 <= pl.n_units / 2 && target >= kw * 1.5) kw *= 2;
+    }
+    int ks = 1;
     auto fits = [&](int ks_) {
         const int umax = (pl.n_units + ks_ - 1) / ks_;
         return smem_map(type, pl.nt, umax, rows).total <= 220 * 1024;
