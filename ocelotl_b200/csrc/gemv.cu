@@ -182,9 +182,21 @@ __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, 
         const int c = 3 * m + sp;
         *reinterpret_cast<uint2*>(p.xq + (int64_t)c * p.kx + k0) = make_uint2(pk[sp][0], pk[sp][1]);
         int s = sum[sp] + __shfl_xor_sync(0xffffffffu, sum[sp], 1);
-        if ((lane & 1) == 0) p.s16[(int64_t)c * (p.kx / 16) + b * 16 + (lane >> 1)] = s;
+        if ((lane & 1) == 0) {
+            const int j = lane >> 1;
+            p.s16[(int64_t)c * (p.kx / 16) + b * 16 + j] = s;
+            int8_t* pc = p.p16 + ((int64_t)c * (p.kx / 256) + b) * 32;
+            pc[j] = (int8_t)(s & 63);        // s = lo + 64 * hi, lo in 0..63
+            pc[16 + j] = (int8_t)(s >> 6);   // |s| <= 2032 -> hi in -32..31
+        }
         s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if ((lane & 3) == 0) p.s32[(int64_t)c * (p.kx / 32) + b * 8 + (lane >> 2)] = s;
+        if ((lane & 3) == 0) {
+            const int j = lane >> 2;
+            p.s32[(int64_t)c * (p.kx / 32) + b * 8 + j] = s;
+            int8_t* pc = p.p32 + ((int64_t)c * (p.kx / 256) + b) * 16;
+            pc[j] = (int8_t)(s & 63);
+            pc[8 + j] = (int8_t)(s >> 6);    // |s| <= 4064 -> hi in -64..63
+        }
     }
     if (lane == 0)
         p.xs[(int64_t)m * (p.kx / 256) + b] =
@@ -194,7 +206,8 @@ __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, 
 // Shared-memory view of the activation planes of one CTA's K range.
 struct XSmem {
     int8_t* q;   // [ncp][qstride]  plane c = 3m + s, natural k order
-    int32_t* s;  // [ncp][sstride]  per-32 (Q4_K) / per-16 (Q6_K) sums of each plane
+    int32_t* s;  // [ncp][sstride]  per-32 (Q4_K) / per-16 (Q6_K) sums of each plane (general layout);
+                 //                 single-row layout: lo/hi byte pieces of those sums, sstride bytes per row
     float* xs;   // [mpad][umax]    block scales 2^e
     int qstride, sstride, umax;
 };
@@ -396,15 +409,16 @@ __device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const 
         lo2 += zext_byte(sc1[j0 >> 2], j0 & 3) * r[2];
         hi2 += zext_byte(sc1[j1 >> 2], j1 & 3) * u[2];
     }
-    const int4* sp = reinterpret_cast<const int4*>(X.s + (t < 3 ? t : 3) * X.sstride + l * 8);
-    const int4 sa0 = sp[0], sa1 = sp[1];
-    const int S[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
-    int M0 = 0, M2 = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        M0 += zext_byte(mn0[j >> 2], j & 3) * S[j];
-        M2 += zext_byte(mn1[j >> 2], j & 3) * S[j];
+    // min term sum_j m_j * S_j on the tensor core: A = mins (k = j, 8 of 16 used),
+    // B column 2p + h = piece h (lo / hi byte) of plane p's sums, so lane t gets
+    // plane t's lo and hi results side by side: M = lo + 64 * hi, exact.
+    int mm[4];
+    {
+        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 3) * X.sstride);
+        const uint32_t bm = t < 2 ? *reinterpret_cast<const uint32_t*>(pr + l * 16 + (g & 1) * 8 + 4 * t) : 0u;
+        mma_s8_k16(mm, t < 2 ? mn0[t & 1] : 0u, t < 2 ? mn1[t & 1] : 0u, bm);
     }
+    const int M0 = mm[0] + 64 * mm[1], M2 = mm[2] + 64 * mm[3];
     const float xs = X.xs[l];
     const float d0 = h2f(h0.x & 0xffffu) * 0.0625f, dm0 = h2f(h0.x >> 16);
     const float d1 = h2f(h1.x & 0xffffu) * 0.0625f, dm1 = h2f(h1.x >> 16);
@@ -427,24 +441,26 @@ __device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const 
     const uint32_t lw[16] = {lo[0].x, lo[0].y, lo[0].z, lo[0].w, lo[1].x, lo[1].y, lo[1].z, lo[1].w,
                              lo[2].x, lo[2].y, lo[2].z, lo[2].w, lo[3].x, lo[3].y, lo[3].z, lo[3].w};
     const uint32_t hw[8] = {hi[0].x, hi[0].y, hi[0].z, hi[0].w, hi[1].x, hi[1].y, hi[1].z, hi[1].w};
-    const int4* sp = reinterpret_cast<const int4*>(X.s + (t < 3 ? t : 3) * X.sstride + l * 16);
     int C0 = 0, C2 = 0;
 #pragma unroll
-    for (int j4 = 0; j4 < 4; ++j4) {
-        const int4 A = sp[j4];
-        const int SA[4] = {A.x, A.y, A.z, A.w};
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            const int j = 4 * j4 + jj;
-            uint32_t a0, a1;
-            q6_frag(j, lw[j], hw[j >> 1], a0, a1);
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
-            int r[4];
-            mma_s8_k16(r, a0, a1, b0);
-            const int off = -32 * SA[jj];
-            C0 += sext_byte(sw0[j >> 2], j & 3) * (r[0] + off);
-            C2 += sext_byte(sw1[j >> 2], j & 3) * (r[2] + off);
-        }
+    for (int j = 0; j < 16; ++j) {
+        uint32_t a0, a1;
+        q6_frag(j, lw[j], hw[j >> 1], a0, a1);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
+        int r[4];
+        mma_s8_k16(r, a0, a1, b0);
+        C0 += sext_byte(sw0[j >> 2], j & 3) * r[0];
+        C2 += sext_byte(sw1[j >> 2], j & 3) * r[2];
+    }
+    // offset term sum_j sc_j * S_j on the tensor core (A = the 16 int8 scales,
+    // B column 2p + h = piece h of plane p's per-16 sums): lo + 64 * hi
+    {
+        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 3) * X.sstride);
+        const uint32_t bm = *reinterpret_cast<const uint32_t*>(pr + l * 32 + (g & 1) * 16 + 4 * t);
+        int mm[4];
+        mma_s8_k16(mm, sw0[t], sw1[t], bm);
+        C0 -= 32 * (mm[0] + 64 * mm[1]);
+        C2 -= 32 * (mm[2] + 64 * mm[3]);
     }
     const float xs = X.xs[l];
     const float d0 = h2f(*reinterpret_cast<const unsigned short*>(rec + 256 + 2 * g));
@@ -483,7 +499,8 @@ struct SmemMap {
 __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows) {
     const int nc = nt * 8, mpad = nt ? (nc + 2) / 3 : 1, ncp = nt ? 3 * mpad : 4;
     const int qstride = umax * 256 + 32;
-    const int sstride = sum_per(type) ? umax * sum_per(type) + 4 : 0;
+    // ints per sum row: 4-byte sums (general layout) or 2 bytes per sum (lo/hi pieces, single row)
+    const int sstride = sum_per(type) ? (nt ? umax * sum_per(type) : umax * sum_per(type) / 2) + 4 : 0;
     SmemMap m;
     m.ring = 0;
     m.bars = kWarps * kStages * unit_bytes(type);
@@ -525,7 +542,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     float* red = reinterpret_cast<float*>(smem + map.red);
     const XSmem X{reinterpret_cast<int8_t*>(smem + map.xq), reinterpret_cast<int32_t*>(smem + map.xsum),
                   reinterpret_cast<float*>(smem + map.xs), a.umax * 256 + 32,
-                  sum_per(TYPE) ? a.umax * sum_per(TYPE) + 4 : 0, a.umax};
+                  sum_per(TYPE) ? (NT ? a.umax * sum_per(TYPE) : a.umax * sum_per(TYPE) / 2) + 4 : 0, a.umax};
 
     auto unit_src = [&](int u, uint32_t& bytes) -> const uint8_t* {
         if (TYPE == kQ8_0) {
@@ -561,15 +578,19 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     pdl_trigger();
     const int NU = U1 - U0;
     if (warp == 0) {
-        const uint32_t qb = (uint32_t)NU * 256, sb = (uint32_t)(NU * sum_per(TYPE) * 4);
+        const uint32_t qb = (uint32_t)NU * 256, sb = (uint32_t)(NU * sum_per(TYPE) * (NT ? 4 : 2));
         if (lane == 0) mbar_expect_tx(xbar, NCP * (qb + sb));
         __syncwarp();
         for (int c = lane; c < NCP; c += 32) {
             bulk_g2s(X.q + c * X.qstride, a.p.xq + (int64_t)c * a.p.kx + (int64_t)U0 * 256, qb, xbar);
-            if (sum_per(TYPE)) {
+            if (sum_per(TYPE) && NT) {
                 const int32_t* src = (TYPE == kQ4_K) ? a.p.s32 : a.p.s16;
                 const int64_t gstride = (int64_t)(a.p.kx / 256) * sum_per(TYPE);
                 bulk_g2s(X.s + c * X.sstride, src + (int64_t)c * gstride + (int64_t)U0 * sum_per(TYPE), sb, xbar);
+            } else if (sum_per(TYPE)) {  // single row: byte pieces of the sums
+                const int8_t* src = (TYPE == kQ4_K) ? a.p.p32 : a.p.p16;
+                const int per = 2 * sum_per(TYPE);
+                bulk_g2s(X.s + c * X.sstride, src + ((int64_t)c * (a.p.kx / 256) + U0) * per, sb, xbar);
             }
         }
     }
@@ -781,6 +802,8 @@ XPlanes xplanes_carve(void* base, int64_t k) {
     p.s16 = (int32_t*)take((size_t)kColsMax * (p.kx / 16) * 4);
     p.s32 = (int32_t*)take((size_t)kColsMax * (p.kx / 32) * 4);
     p.xs = (float*)take((size_t)kRowsMax * (p.kx / 256) * 4);
+    p.p32 = (int8_t*)take((size_t)kColsMax * (p.kx / 256) * 16);
+    p.p16 = (int8_t*)take((size_t)kColsMax * (p.kx / 256) * 32);
     return p;
 }
 

@@ -18,6 +18,8 @@ struct XPlanes {
     int32_t* s16;  // [kColsMax][kx/16]
     int32_t* s32;  // [kColsMax][kx/32]
     float* xs;     // [kRowsMax][kx/256]
+    int8_t* p32;   // [kColsMax][kx/256][16]: per-32 sums as lo (0..63) / hi bytes, sum = lo + 64*hi
+    int8_t* p16;   // [kColsMax][kx/256][32]: per-16 sums, same split
     int kx;        // K rounded up to a multiple of 256
 };
 
@@ -25,13 +27,13 @@ constexpr int kRowsMax = 16;            // activation rows per GEMV launch
 constexpr int kColsMax = 3 * kRowsMax;  // int8 planes per launch
 
 // Bytes of scratch the x planes need for a given K.
-inline size_t xplanes_bytes(int64_t k) {
-    const int64_t kx = (k + 255) / 256 * 256;
-    return (size_t)kColsMax * kx               // xq
-           + (size_t)kColsMax * (kx / 16) * 4  // s16
-           + (size_t)kColsMax * (kx / 32) * 4  // s32
-           + (size_t)kRowsMax * (kx / 256) * 4 // xs
-           + 4 * 256;                          // alignment slack
+constexpr size_t xplanes_bytes(int64_t k) {
+    return (size_t)kColsMax * ((k + 255) / 256 * 256)     // xq
+           + (size_t)kColsMax * ((k + 255) / 256 * 16) * 4  // s16
+           + (size_t)kColsMax * ((k + 255) / 256 * 8) * 4   // s32
+           + (size_t)kRowsMax * ((k + 255) / 256) * 4       // xs
+           + (size_t)kColsMax * ((k + 255) / 256) * 48      // p32 + p16
+           + 6 * 256;                                       // alignment slack
 }
 // Carve the planes out of one scratch allocation (256-byte aligned pieces).
 XPlanes xplanes_carve(void* base, int64_t k);

@@ -24,9 +24,7 @@ namespace {
 
 constexpr int64_t kMaxK = 16384;
 constexpr size_t kScratchBytes = 4u << 20;
-constexpr size_t kPlanesBytes = (ocl::kColsMax * kMaxK + ocl::kColsMax * (kMaxK / 16) * 4 +
-                                 ocl::kColsMax * (kMaxK / 32) * 4 + ocl::kRowsMax * (kMaxK / 256) * 4 + 4 * 256 +
-                                 255) / 256 * 256;
+constexpr size_t kPlanesBytes = (ocl::xplanes_bytes(kMaxK) + 255) / 256 * 256;
 constexpr size_t kMaxGroups = 4096;
 constexpr size_t kCounterBytes = (kMaxGroups + 64) * sizeof(unsigned int);  // counters, then 2 error flags
 constexpr size_t kPartBytes = kScratchBytes - kPlanesBytes - kCounterBytes;
