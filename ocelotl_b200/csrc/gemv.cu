@@ -28,9 +28,11 @@
 //  * Narrow matrices also split K across CTAs; those partial sums go through
 //    scratch memory and the last CTA of each row group adds them in split order
 //    (one counter per group).  Every reduction has a fixed order: deterministic.
-//  * Both kernels launch with programmatic dependent launch: the GEMV's weight
-//    stream starts before griddepcontrol.wait, overlapping its predecessors;
-//    planes, partials and counters are touched only after the wait.
+//  * Both kernels launch with programmatic dependent launch and the split
+//    kernel releases its dependent at once, so a GEMV starts while its
+//    predecessors run and fills its rings before griddepcontrol.wait; planes,
+//    partials and counters are touched only after the wait.  (Prefetching the
+//    whole weight slice into L2 there measured slower and is not done.)
 //  * Every mbarrier wait is bounded; a wait that gives up bumps an error counter
 //    the host reads (ocl_take_device_errors), drains its own copies and returns.
 #include <cuda_fp16.h>
@@ -133,8 +135,11 @@ __device__ __forceinline__ int zext_byte(uint32_t w, int i) {
 // zeros (they feed idle MMA columns).  |x / xs| < 2^7 with xs = 2^e per block.
 // ---------------------------------------------------------------------------
 __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, XPlanes p) {
-    pdl_wait();  // x is the previous kernel's output; planes may still be read by it
+    // Let the GEMV that follows launch now: it only streams weights until it
+    // waits for this kernel.  This kernel itself must wait for its predecessor:
+    // x is that kernel's output and the planes may still be read by it.
     pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x, m = blockIdx.y, lane = threadIdx.x;
     const int64_t k0 = (int64_t)b * 256 + lane * 8;
     float v[8];
@@ -377,13 +382,21 @@ __device__ __forceinline__ void consume_q80(const uint8_t* rec, int l, int nb, c
 
 // ---- single activation row (M = 1) -----------------------------------------
 // The three planes sit in MMA columns 0, 2 and 4 (lane t's even column 2t holds
-// plane t for t < 3); odd columns and column 6 read a zero row.  Each lane then
+// plane t for t < 3); the other columns' B fragments are zero registers.  Each lane then
 // keeps only its two useful accumulators (rows g and g+8, plane t).
-__device__ __forceinline__ int m1_bplane(int g) { return ((g & 1) == 0 && g < 6) ? (g >> 1) : 3; }
+__device__ __forceinline__ int m1_bplane(int g) { return ((g & 1) == 0 && g < 6) ? (g >> 1) : 0; }
+__device__ __forceinline__ bool m1_bidle(int g) { return (g & 1) || g >= 6; }  // MMA column reads zeros
+__device__ __forceinline__ uint32_t ld_b32(const int8_t* p, bool idle) {
+    return idle ? 0u : *reinterpret_cast<const uint32_t*>(p);
+}
+__device__ __forceinline__ uint2 ld_b64(const int8_t* p, bool idle) {
+    return idle ? make_uint2(0u, 0u) : *reinterpret_cast<const uint2*>(p);
+}
 
 __device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const XSmem& X, float& acc0,
                                                float& acc2, int g, int t, int lane) {
     const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 8 * t;
+    const bool bidle = m1_bidle(g);
     const uint4 h0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
     const uint4 h1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
     uint4 q[4];
@@ -396,8 +409,8 @@ __device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const 
     int lo0 = 0, hi0 = 0, lo2 = 0, hi2 = 0;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        const uint2 bl = *reinterpret_cast<const uint2*>(xb + 64 * c);
-        const uint2 bh = *reinterpret_cast<const uint2*>(xb + 64 * c + 32);
+        const uint2 bl = ld_b64(xb + 64 * c, bidle);
+        const uint2 bh = ld_b64(xb + 64 * c + 32, bidle);
         int r[4], u[4];
         mma_s8_k32(r, q[c].x & 0x0F0F0F0Fu, q[c].z & 0x0F0F0F0Fu, q[c].y & 0x0F0F0F0Fu, q[c].w & 0x0F0F0F0Fu, bl.x,
                    bl.y);
@@ -414,8 +427,8 @@ __device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const 
     // plane t's lo and hi results side by side: M = lo + 64 * hi, exact.
     int mm[4];
     {
-        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 3) * X.sstride);
-        const uint32_t bm = t < 2 ? *reinterpret_cast<const uint32_t*>(pr + l * 16 + (g & 1) * 8 + 4 * t) : 0u;
+        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 0) * X.sstride);
+        const uint32_t bm = ld_b32(pr + l * 16 + (g & 1) * 8 + 4 * t, t >= 2 || g >= 6);
         mma_s8_k16(mm, t < 2 ? mn0[t & 1] : 0u, t < 2 ? mn1[t & 1] : 0u, bm);
     }
     const int M0 = mm[0] + 64 * mm[1], M2 = mm[2] + 64 * mm[3];
@@ -429,6 +442,7 @@ __device__ __forceinline__ void consume_q4k_m1(const uint8_t* rec, int l, const 
 __device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const XSmem& X, float& acc0,
                                                float& acc2, int g, int t, int lane) {
     const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 4 * t;
+    const bool bidle = m1_bidle(g);
     const uint4 s0 = *reinterpret_cast<const uint4*>(rec + 16 * g);
     const uint4 s1 = *reinterpret_cast<const uint4*>(rec + 16 * (g + 8));
     uint4 lo[4], hi[2];
@@ -446,7 +460,7 @@ __device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const 
     for (int j = 0; j < 16; ++j) {
         uint32_t a0, a1;
         q6_frag(j, lw[j], hw[j >> 1], a0, a1);
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
+        const uint32_t b0 = ld_b32(xb + 16 * j, bidle);
         int r[4];
         mma_s8_k16(r, a0, a1, b0);
         C0 += sext_byte(sw0[j >> 2], j & 3) * r[0];
@@ -455,8 +469,8 @@ __device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const 
     // offset term sum_j sc_j * S_j on the tensor core (A = the 16 int8 scales,
     // B column 2p + h = piece h of plane p's per-16 sums): lo + 64 * hi
     {
-        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 3) * X.sstride);
-        const uint32_t bm = *reinterpret_cast<const uint32_t*>(pr + l * 32 + (g & 1) * 16 + 4 * t);
+        const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (g < 6 ? (g >> 1) : 0) * X.sstride);
+        const uint32_t bm = ld_b32(pr + l * 32 + (g & 1) * 16 + 4 * t, g >= 6);
         int mm[4];
         mma_s8_k16(mm, sw0[t], sw1[t], bm);
         C0 -= 32 * (mm[0] + 64 * mm[1]);
@@ -472,14 +486,15 @@ __device__ __forceinline__ void consume_q6k_m1(const uint8_t* rec, int l, const 
 __device__ __forceinline__ void consume_q80_m1(const uint8_t* rec, int l, int nb, const XSmem& X, float& acc0,
                                                float& acc2, int g, int t, int lane) {
     const int8_t* xb = X.q + m1_bplane(g) * X.qstride + l * 256 + 4 * t;
+    const bool bidle = m1_bidle(g);
     float b0 = 0.f, b2 = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         if (i < nb) {
             const uint8_t* r8 = rec + 544 * i;
             const uint4 q = *reinterpret_cast<const uint4*>(r8 + 32 + 16 * lane);
-            const uint32_t bx = *reinterpret_cast<const uint32_t*>(xb + 32 * i);
-            const uint32_t by = *reinterpret_cast<const uint32_t*>(xb + 32 * i + 16);
+            const uint32_t bx = ld_b32(xb + 32 * i, bidle);
+            const uint32_t by = ld_b32(xb + 32 * i + 16, bidle);
             int r[4];
             mma_s8_k32(r, q.x, q.y, q.z, q.w, bx, by);
             b0 += h2f(*reinterpret_cast<const unsigned short*>(r8 + 2 * g)) * (float)r[0];
@@ -492,12 +507,12 @@ __device__ __forceinline__ void consume_q80_m1(const uint8_t* rec, int l, int nb
 }
 
 // Shared-memory carve-up of one CTA (host and device agree on it).  nt == 0 is
-// the single-row layout: planes 0..2 plus a zero row for idle MMA columns.
+// the single-row layout: planes 0..2 and the byte pieces of their sums.
 struct SmemMap {
     int ring, bars, red, xq, xsum, xs, total;
 };
 __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows) {
-    const int nc = nt * 8, mpad = nt ? (nc + 2) / 3 : 1, ncp = nt ? 3 * mpad : 4;
+    const int nc = nt * 8, mpad = nt ? (nc + 2) / 3 : 1, ncp = 3 * mpad;
     const int qstride = umax * 256 + 32;
     // ints per sum row: 4-byte sums (general layout) or 2 bytes per sum (lo/hi pieces, single row)
     const int sstride = sum_per(type) ? (nt ? umax * sum_per(type) : umax * sum_per(type) / 2) + 4 : 0;
@@ -598,11 +613,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
         const int m = i / NU, o = i - m * NU;
         X.xs[m * X.umax + o] = a.p.xs[(int64_t)m * (a.p.kx / 256) + U0 + o];
     }
-    if (NT == 0) {  // zero row read by idle MMA columns
-        for (int i = threadIdx.x; i < X.qstride / 16; i += blockDim.x)
-            reinterpret_cast<uint4*>(X.q + 3 * X.qstride)[i] = make_uint4(0, 0, 0, 0);
-        for (int i = threadIdx.x; i < X.sstride; i += blockDim.x) X.s[3 * X.sstride + i] = 0;
-    }
     bool ok = mbar_wait_bounded(xbar, 0);
     __syncthreads();
 
@@ -622,6 +632,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
             }
             const uint8_t* rec = ring + st * UB;
             const int l = u0 + done - U0;
+#ifdef OCL_GEMV_PROBE_NOCOMPUTE
+            if (rec[lane] == 0xEE && l < 0) acc[0][0] += 1.f;  // data-movement ceiling experiment
+            else
+#endif
             if constexpr (NT == 0) {
                 if (TYPE == kQ4_K) consume_q4k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
                 else if (TYPE == kQ6_K) consume_q6k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
@@ -765,6 +779,8 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
     if (rows <= 2) {
         const double target = 1536.0 * sms / 148.0 / (double)pl.n_rt;
         while (kw < 4 && kw * 2 <= pl.n_units / 2 && target >= kw * 1.5) kw *= 2;
+        // never leave SMs without a CTA
+        while (kw < kWarps && kw * 2 <= pl.n_units / 2 && (pl.n_rt + kWarps / kw - 1) / (kWarps / kw) < sms) kw *= 2;
     }
     int ks = 1;
     auto fits = [&](int ks_) {
