@@ -213,6 +213,7 @@ def run_ocelotl(args):
     from ocelotl_b200 import synth
     from ocelotl_b200.backend import CudaKernelBackend
     from ocelotl_b200.build import build
+    from ocelotl_b200.tp import TPLinear
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -235,9 +236,10 @@ def run_ocelotl(args):
     weights = []
     for c in range(copies):
         ws = {}
-        for name, t, n, k, _ in shards:
+        for name, t, n, k, sp in shards:
+            # this rank's shard, generated in place (same distribution as a sharded full weight)
             blocks = synth.quant_blocks(t, n, k, args.seed, f"{name}.r{rank}.c{c}", device=dev)
-            ws[name] = be.upload_quant(t, blocks, n, k)
+            ws[name] = TPLinear(be, t, blocks, n, k, "out" if sp == "col" else "in")
             del blocks
         weights.append(ws)
     torch.cuda.synchronize()
@@ -249,9 +251,7 @@ def run_ocelotl(args):
     def step(c):
         ws = weights[c]
         for name, t, n, k, sp in shards:
-            be.linear_dev(ws[name], xs[xin[name]], m, ys[name])
-            if sp == "row" and tp > 1:
-                dist.all_reduce(ys[name])
+            ws[name].forward(xs[xin[name]], m, ys[name])
 
     # ---- device-resident timing: one graph per weight copy --------------------
     if tp == 1:
@@ -288,7 +288,7 @@ def run_ocelotl(args):
     proj = {}
     reps = 2 * copies
     for name, t, n, k, sp in shards:
-        g = graph_of(lambda name=name: [be.linear_dev(weights[r % copies][name], xs[xin[name]], m, ys[name])
+        g = graph_of(lambda name=name: [be.linear_dev(weights[r % copies][name].weight, xs[xin[name]], m, ys[name])
                                         for r in range(reps)], be, torch)
         g.replay()
         torch.cuda.synchronize()
@@ -324,7 +324,8 @@ def run_ocelotl(args):
     def e2e_step(i):
         ws = weights[i % copies]
         for name, t, n, k, sp in shards:
-            be.linear_out_by_in(pinned_x[xin[name]].numpy(), m, k, ws[name], n, None, pinned_y[name].numpy())
+            be.linear_out_by_in(pinned_x[xin[name]].numpy(), m, k, ws[name].weight, n, None,
+                                pinned_y[name].numpy())
             if sp == "row" and tp > 1:
                 y = pinned_y[name].to(dev)
                 dist.all_reduce(y)
@@ -355,7 +356,7 @@ def run_ocelotl(args):
 
             def sstep(c, mm=mm, xm=xm, ym=ym):
                 for nm in sh:
-                    be.linear_dev(weights[c][nm], xm[xin[nm]], mm, ym[nm])
+                    be.linear_dev(weights[c][nm].weight, xm[xin[nm]], mm, ym[nm])
             gs = [graph_of(lambda c=c: sstep(c), be, torch) for c in range(copies)]
             for i in range(3):
                 gs[i % copies].replay()
