@@ -221,7 +221,8 @@ def run_ocelotl(args):
     torch.cuda.set_device(local if world > 1 else 0)
     dev = torch.device("cuda", torch.cuda.current_device())
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
     if rank == 0:
         build()
     if world > 1:
@@ -254,11 +255,13 @@ def run_ocelotl(args):
             ws[name].forward(xs[xin[name]], m, ys[name])
 
     # ---- device-resident timing: one graph per weight copy --------------------
-    if tp == 1:
-        graphs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
-        run = lambda i: graphs[i % copies].replay()  # noqa: E731
-    else:
-        run = lambda i: step(i % copies)  # noqa: E731  (NCCL inside: eager launches)
+    if tp > 1:
+        for c in range(copies):  # NCCL communicators and buffers set up before capture
+            step(c)
+        torch.cuda.synchronize()
+        dist.barrier()
+    graphs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
+    run = lambda i: graphs[i % copies].replay()  # noqa: E731
     for i in range(args.warmup):
         run(i)
     torch.cuda.synchronize()
@@ -391,7 +394,8 @@ def run_ocelotl(args):
                              f"({copies * rank_wbytes / 1e6:.0f} MB per GPU, >= 4x the 126 MB L2)",
                        "alg_bytes_per_step": layer_alg_bytes(m),
                        "pct_of_8TBps": round(100 * gbs / 8000.0, 2),
-                       "step": "CUDA graph of 5 ocl_q_linear calls" if tp == 1 else "eager calls + NCCL all-reduce"},
+                       "step": "CUDA graph of 5 ocl_q_linear calls" + ("" if tp == 1 else
+                                                                          " + 2 NCCL all-reduces (o, down)")},
             "roofline": roofline,
             "projections": proj,
             "cpu_baseline": cpu,
@@ -409,8 +413,14 @@ def run_ocelotl(args):
             line["m_sweep"] = sweep
         print(json.dumps(line), flush=True)
     if world > 1:
+        # Leave without tearing the process group down: graphs captured with
+        # NCCL work can block destroy_process_group at exit.
+        del graphs
+        torch.cuda.synchronize()
         dist.barrier()
-        dist.destroy_process_group()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     return 0
 
 
