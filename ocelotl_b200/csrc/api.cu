@@ -424,8 +424,21 @@ int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_dev, size
                     size_t out_features, uint16_t* y_dev) {
     if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    (void)w; (void)x_dev; (void)rows; (void)in_features; (void)out_features; (void)y_dev;
-    return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `q_gemm_bf16`: supported = []");
+    int rc = check_linear_shapes(ctx, w, rows, in_features, out_features);
+    if (rc) return rc;
+    if (in_features % 256 != 0)
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `q_gemm_bf16 in_features` (requested `%zu`): supported = [multiples of 256]",
+                    in_features);
+    if (!x_dev || !y_dev) return fail(ctx, OCL_ERR_INVALID, "q_gemm_bf16 x/out pointer is null");
+    if (((uintptr_t)x_dev & 15) != 0)
+        return fail(ctx, OCL_ERR_INVALID, "q_gemm_bf16 x must be 16-byte aligned");
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx,
+             ocl::launch_qgemm(w->type, w->dev, (int64_t)rows, (int64_t)out_features, (int64_t)in_features, x_dev,
+                               y_dev, ctx->dev_flags, ctx->stream),
+             "q_gemm launch");
+    return OCL_OK;
 }
 
 }  // extern "C"

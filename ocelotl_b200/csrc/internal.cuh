@@ -81,4 +81,8 @@ cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
                         unsigned int* err, bool pdl, cudaStream_t s);
 
+// Prefill GEMM: y bf16 [M, N] = x bf16 [M, K] . W^T on tcgen05 (K a multiple of 256).
+cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
+                         uint16_t* y, unsigned int* err, cudaStream_t s);
+
 }  // namespace ocl
