@@ -3,15 +3,16 @@
 // y[m, n] (bf16) = sum_k x[m, k] (bf16) * W[n, k], W GGUF-quantized in TILED16
 // records, f32 accumulation in tensor memory.
 //
-// One CTA computes a 128 (tokens) x 128 (output features) tile:
-//   * warp 8 (one lane) streams x tiles [128 x 64] bf16 with TMA (tiled,
+// One CTA computes a 256 (tokens) x 128 (output features) tile as two 128 x 128
+// accumulators in tensor memory that share each dequantized weight tile:
+//   * warp 8 (one lane) streams x tiles [256 x 64] bf16 with TMA (tiled,
 //     128-byte swizzle, no multicast) into a 4-stage shared-memory ring;
 //   * warps 0-7 dequantize the matching weight tile [128 features x 64 k] from
 //     the TILED16 records (prefetched one 256-k unit ahead in registers) into
 //     bf16, written directly in the 128-byte-swizzled K-major layout the UMMA
 //     descriptors describe; each value is d*sc*q - dmin*m (Q4_K),
 //     d*sc*(q-32) (Q6_K) or d*q (Q8_0) in f32, rounded to bf16;
-//   * warp 9 allocates 128 TMEM columns and one lane issues
+//   * warp 9 allocates 256 TMEM columns and one lane issues
 //     tcgen05.mma.cta_group::1.kind::f16 (M=128, N=128, K=16, A and B K-major),
 //     releasing each stage with tcgen05.commit to an mbarrier;
 //   * warps 0-3 read the accumulator with tcgen05.ld (32 lanes x 32 columns per
@@ -28,8 +29,9 @@ namespace ocl {
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;  // 16 KB each
+constexpr int BM = 256, BN = 128, BK = 64, STAGES = 4;       // BM = two 128-row MMA tiles sharing B
+constexpr int MMA_M = 128, ACCS = BM / MMA_M;                  // accumulators in TMEM (BN columns each)
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;  // 32 KB + 16 KB per stage
 constexpr int PRODUCER_WARPS = 8, TMA_WARP = 8, MMA_WARP = 9, THREADS = 320;
 constexpr long long kWaitCycles = 2000000000LL;
 
@@ -72,7 +74,7 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor: f32 accumulator, bf16 A and B, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MMA_M >> 4) << 24);
 
 __device__ __forceinline__ void umma(uint32_t dtmem, uint64_t ad, uint64_t bd, uint32_t accumulate) {
     asm volatile(
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (warp == MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
-                     "r"(BN));
+                     "r"(ACCS * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -348,7 +350,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t a_base = sa(atiles + s * A_BYTES), b_base = sa(btiles + s * B_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk)
-                    umma(tmem, umma_desc(a_base + 32 * kk), umma_desc(b_base + 32 * kk), (kb | kk) != 0);
+#pragma unroll
+                    for (int acc = 0; acc < ACCS; ++acc)  // 128-row A halves, 16 KB apart
+                        umma(tmem + acc * BN, umma_desc(a_base + acc * (MMA_M * 128) + 32 * kk),
+                             umma_desc(b_base + 32 * kk), (kb | kk) != 0);
                 umma_commit(&empty[s]);
             }
             umma_commit(done);  // arrives once every MMA issued above has completed
@@ -361,11 +366,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) atomicExch(&abort_flag_s, 1);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__all_sync(0xffffffffu, ok && !abort_flag)) {
-            const int64_t m = m0 + 32 * warp + lane;
+#pragma unroll 1
+            for (int acc = 0; acc < ACCS; ++acc) {
+            const int64_t m = m0 + acc * MMA_M + 32 * warp + lane;
 #pragma unroll
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t v[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0;
+                const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(acc * BN + c0);
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -392,6 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -399,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0 && abort_flag) atomicAdd(err + 1, 1u);
     if (warp == MMA_WARP) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ACCS * BN));
     }
 }
 
@@ -443,7 +451,7 @@ cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int6
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t box[2] = {BK, BM};  // one 64 x 256 bf16 box = both 128-row halves
     const cuuint32_t estr[2] = {1, 1};
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
