@@ -42,7 +42,7 @@ LAYER = [
     ("up", Q4_K, FFN, HIDDEN, "col"),
     ("down", Q6_K, HIDDEN, FFN, "row"),
 ]
-BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210)}
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), 8: (32, 34)}
 L2_BYTES = 126 * 2**20
 METRIC = "Q4_K/Q6_K GEMV HBM GB/s (% of 8 TB/s); 8B-shape decode tok/s @1/2/4/8"
 WORKLOAD = "llama3-8b-shape decoder layer, all linear projections (qkv/o/gate/up Q4_K, down Q6_K)"
@@ -204,6 +204,103 @@ def graph_of(fn, be, torch):
     be.set_stream(None)
     torch.cuda.synchronize()
     return g
+
+
+def bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured burst cuBLAS bf16"
+    return 1590.0, "fallback"
+
+
+def run_prefill(be, ws, sh, args, torch):
+    """the 8B layer's five projections as bf16 tcgen05 GEMMs, M = 512 and 2048 tokens."""
+    from ocelotl_b200 import synth
+    out = {}
+    peak, src = bf16_peak()
+    for M in (512, 2048):
+        xs = {nm: synth.activations(M, sh[nm][2], args.seed, f"px.{nm}", device="cuda",
+                                    dtype=torch.bfloat16).contiguous() for nm in sh}
+        ys = {nm: torch.empty(M, sh[nm][1], device="cuda", dtype=torch.bfloat16) for nm in sh}
+        xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+
+        def layer():
+            for nm in sh:
+                be.gemm_bf16(xs[xin[nm]], ws[nm].weight, ys[nm])
+        g = graph_of(layer, be, torch)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(b) / reps
+        flops = 2 * M * sum(n * k for _, n, k, _ in sh.values())
+        tf = flops / (us * 1e-6) / 1e12
+        out[str(M)] = {"layer_us": round(us, 1), "TFLOP/s": round(tf, 1), "frac": round(tf / peak, 4),
+                       "flops": flops}
+        del g
+    out["peak"] = {"TFLOP/s": peak, "source": src}
+    out["kernel"] = "qgemm_kernel: tcgen05.mma kind::f16, 256x128 CTA tile, weights dequantized to bf16 in smem"
+    return out
+
+
+def run_stack(be, args, torch, synth, dev):
+    """32 decoder layers' projections + Q6_K output head + Q8_0 embedding rows, per decode token."""
+    n_layers, vocab = 32, 128256
+    layers = []
+    for li in range(n_layers):
+        ws = {}
+        for name, t, n, k, _ in LAYER:
+            blocks = synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.{name}", device=dev)
+            ws[name] = be.upload_quant(t, blocks, n, k)
+            del blocks
+        layers.append(ws)
+    head = be.upload_quant(Q6_K, synth.quant_blocks(Q6_K, vocab, HIDDEN, args.seed, "stack.head", device=dev),
+                           vocab, HIDDEN)
+    emb = be.upload_quant(8, synth.quant_blocks(8, vocab, HIDDEN, args.seed, "stack.emb", device=dev), vocab, HIDDEN)
+    torch.cuda.synchronize()
+    res = {}
+    wbytes_total = n_layers * sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER) + wbytes(Q6_K, vocab, HIDDEN)
+    for m in (1, 8):
+        ids = torch.randint(0, vocab, (m,), dtype=torch.int32, device=dev)
+        h = torch.empty(m, HIDDEN, device=dev)
+        xs = {name: synth.activations(m, k, args.seed, f"stack.x.{name}", device=dev) for name, t, n, k, _ in LAYER}
+        ys = {name: torch.empty(m, n, device=dev) for name, t, n, k, _ in LAYER}
+        logits = torch.empty(m, vocab, device=dev)
+        xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+
+        def token():
+            be.embed_rows(emb, ids, h)
+            for ws in layers:
+                for name, t, n, k, _ in LAYER:
+                    be.linear_dev(ws[name], xs[xin[name]], m, ys[name])
+            be.linear_dev(head, h, m, logits)
+        g = graph_of(token, be, torch)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(b) / reps
+        alg = wbytes_total + m * wbytes(8, 1, HIDDEN)
+        res[str(m)] = {"token_us": round(us, 1), "tok_s": round(m / (us * 1e-6), 1),
+                       "GB/s": round(alg / (us * 1e-6) / 1e9, 1), "alg_bytes": alg}
+        del g
+    res["note"] = ("per decode step: Q8_0 embedding gather, 32 x (qkv, o, gate, up, down) quantized GEMVs and the "
+                   "Q6_K output head, one CUDA graph; linear layers only (no attention or norms)")
+    del layers, head, emb
+    torch.cuda.synchronize()
+    return res
 
 
 def run_ocelotl(args):
@@ -378,6 +475,8 @@ def run_ocelotl(args):
                               "tok_s_layer": round(mm / (us * 1e-6), 1)}
             del gs
 
+    prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
+    stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
     errs = be.take_device_errors()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,6 +510,10 @@ def run_ocelotl(args):
         }
         if sweep:
             line["m_sweep"] = sweep
+        if prefill:
+            line["prefill_gemm"] = prefill
+        if stack:
+            line["linear_stack_8b"] = stack
         print(json.dumps(line), flush=True)
     if world > 1:
         # Leave without tearing the process group down: graphs captured with
@@ -434,6 +537,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0x0CE107)
     ap.add_argument("--sweep", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
+    ap.add_argument("--stack", type=int, default=1, help="also time configs[3] (8B linear stack per token)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
