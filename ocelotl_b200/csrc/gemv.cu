@@ -783,6 +783,24 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
         while (kw < kWarps && kw * 2 <= pl.n_units / 2 && (pl.n_rt + kWarps / kw - 1) / (kWarps / kw) < sms) kw *= 2;
     }
     int ks = 1;
+    if (rows > 2) {
+        // Batched decode (measured on B200, Llama-shaped matrices, M = 4..16): the
+        // staged activation planes grow with M, so wide matrices keep 8 row
+        // tiles per CTA, deep ones (K >= 8192) split K across 4-8 CTAs to keep
+        // the planes small, and narrow ones split K 2-4 ways inside the CTA.
+        if (pl.n_rt >= 768) {
+            kw = 1;
+        } else if (pl.n_units >= 32) {
+            kw = 1;
+            ks = rows <= 8 ? 4 : 8;
+        } else if (rows <= 8) {
+            kw = pl.n_rt <= 256 ? 4 : 2;
+        } else {
+            kw = pl.n_rt <= 256 ? 2 : 1;
+        }
+        while (kw > 1 && kw > pl.n_units / 2) kw /= 2;
+        if (ks > pl.n_units) ks = pl.n_units;
+    }
     auto fits = [&](int ks_) {
         const int umax = (pl.n_units + ks_ - 1) / ks_;
         return smem_map(type, pl.nt, umax, rows).total <= 220 * 1024;
