@@ -64,6 +64,7 @@ enum { OCL_LAYOUT_GGUF = 0, OCL_LAYOUT_TILED16 = 1 };
 
 typedef struct ocl_ctx ocl_ctx;   /* one device + stream + scratch */
 typedef struct ocl_qbuf ocl_qbuf; /* a quantized weight resident in HBM */
+typedef struct ocl_tpcomm ocl_tpcomm; /* tensor-parallel peer buffers of one rank */
 
 /* ---- context ------------------------------------------------------------ */
 
@@ -135,6 +136,30 @@ OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, si
 OCL_API int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size_t rows,
                       size_t in_features, size_t out_features, const float* bias_host,
                       float* y_host);
+
+/* ---- tensor parallelism (one process per GPU) ----------------------------- */
+/* The reference has no multi-device code (Device::Gpu{ordinal} names one GPU,
+ * crates/core/src/lib.rs:437-441); these entry points are new.
+ * ocl_tp_comm_create allocates this rank's receive buffer (2 x world x max_elems
+ * f32 plus world x max_groups flags) and writes its 64-byte CUDA IPC handle to
+ * ipc_handle_out; the caller gathers all ranks' handles (in rank order, e.g.
+ * with torch.distributed all_gather) and passes them to ocl_tp_comm_open, which
+ * maps the peers' buffers (NVLink / NVSwitch peer memory).  A handle equal to
+ * this rank's own maps that slot back onto this rank's buffer (loopback, used
+ * to exercise the bounded wait without a second process). */
+OCL_API int ocl_tp_comm_create(ocl_ctx* ctx, int rank, int world, size_t max_elems, size_t max_groups,
+                               ocl_tpcomm** out, void* ipc_handle_out);
+OCL_API int ocl_tp_comm_open(ocl_ctx* ctx, ocl_tpcomm* comm, const void* ipc_handles);
+OCL_API int ocl_tp_comm_destroy(ocl_tpcomm* comm);
+/* Row-split quantized linear with the all-reduce fused into the GEMV: each rank
+ * holds W[:, k0:k1] and x[:, k0:k1]; every rank's y receives the sum over ranks
+ * (plus bias), identical bits on every rank.  Each CTA pushes its rows to every
+ * peer, signals a per-row-group flag and waits (bounded, ~1 s; a timeout is
+ * counted by ocl_take_device_errors and leaves y unwritten) for the peers'
+ * rows.  Every rank must issue the same sequence of these calls. */
+OCL_API int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* comm, const ocl_qbuf* w, const float* x_dev,
+                                   size_t rows, size_t in_features, size_t out_features, const float* bias_dev,
+                                   float* y_dev);
 
 /* Allocation-free variant of ocl_q_linear, for callers that cannot allocate
  * GPU memory on the hot path: code running inside someone else's memory pool

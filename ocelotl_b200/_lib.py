@@ -40,6 +40,10 @@ SIGNATURES = {
     "ocl_q_download_gguf": (C.c_int, [_vp, _vp, _vp]),
     "ocl_q_linear": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_linear_noalloc": (C.c_int, [C.c_int, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
+    "ocl_tp_comm_create": (C.c_int, [_vp, C.c_int, C.c_int, _sz, _sz, C.POINTER(_vp), _vp]),
+    "ocl_tp_comm_open": (C.c_int, [_vp, _vp, _vp]),
+    "ocl_tp_comm_destroy": (C.c_int, [_vp]),
+    "ocl_q_linear_allreduce": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_linear_host": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_gemm_bf16": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "ocl_q_embed_rows": (C.c_int, [_vp, _vp, _vp, _sz, _vp]),

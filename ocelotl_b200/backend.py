@@ -310,6 +310,14 @@ class CudaKernelBackend:
     def take_bad_ids(self) -> int:
         return self.take_device_errors()[0]
 
+    def linear_allreduce(self, comm, weight, x: torch.Tensor, rows: int, out: torch.Tensor,
+                         bias: torch.Tensor | None = None) -> None:
+        """Row-split linear with the cross-rank sum fused into the GEMV (see ocelotl_b200.tp.TPComm)."""
+        w = self._quant_weight(weight)
+        self._check(self._lib.ocl_q_linear_allreduce(
+            self._ctx, comm.handle, w.handle, C.c_void_p(x.data_ptr()), rows, w.k, w.n_rows,
+            C.c_void_p(bias.data_ptr()) if bias is not None else None, C.c_void_p(out.data_ptr())))
+
     def set_pdl(self, enable: bool) -> None:
         self._check(self._lib.ocl_set_pdl(self._ctx, 1 if enable else 0))
 

@@ -29,6 +29,15 @@ struct ocl_ctx {
     unsigned int* dev_flags = nullptr;  // [0] bad embedding ids, [1] bounded waits that gave up
 };
 
+struct ocl_tpcomm {
+    int device = 0, world = 1, rank = 0;
+    int64_t max_elems = 0, max_groups = 0;
+    void* buf = nullptr;  // this rank's buffer
+    size_t bytes = 0;
+    void* peer[ocl::kTpMax] = {};  // every rank's buffer as mapped here (own = buf)
+    bool open = false;
+};
+
 struct ocl_qbuf {
     int device = 0;
     int type = 0;
@@ -410,6 +419,116 @@ int ocl_take_device_errors(ocl_ctx* ctx, unsigned int* bad_ids, unsigned int* ti
     OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     if (bad_ids) *bad_ids = h[0];
     if (timeouts) *timeouts = h[1];
+    return OCL_OK;
+}
+
+int ocl_tp_comm_create(ocl_ctx* ctx, int rank, int world, size_t max_elems, size_t max_groups, ocl_tpcomm** out,
+                       void* ipc_handle_out) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!out || !ipc_handle_out) return fail(ctx, OCL_ERR_INVALID, "tp_comm_create: null output pointer");
+    *out = nullptr;
+    if (world < 2 || world > ocl::kTpMax || rank < 0 || rank >= world)
+        return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `tensor-parallel world` (requested `%d`, rank %d): "
+                    "supported = [2..%d]", world, rank, ocl::kTpMax);
+    if (max_elems == 0 || max_groups == 0) return fail(ctx, OCL_ERR_INVALID, "tp_comm_create: zero capacity");
+    DeviceGuard guard(ctx->device);
+    ocl_tpcomm* c = new ocl_tpcomm();
+    c->device = ctx->device;
+    c->world = world;
+    c->rank = rank;
+    c->max_elems = (int64_t)max_elems;
+    c->max_groups = (int64_t)max_groups;
+    c->bytes = ocl::tp_buffer_bytes(world, c->max_elems, c->max_groups);
+    cudaError_t e = cudaMalloc(&c->buf, c->bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->buf, 0, c->bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle_out), c->buf);
+    if (e != cudaSuccess) {
+        if (c->buf) cudaFree(c->buf);
+        delete c;
+        return cuda_fail(ctx, e, "tp_comm_create");
+    }
+    c->peer[rank] = c->buf;
+    *out = c;
+    return OCL_OK;
+}
+
+int ocl_tp_comm_open(ocl_ctx* ctx, ocl_tpcomm* c, const void* handles) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!c || !handles) return fail(ctx, OCL_ERR_INVALID, "tp_comm_open: null argument");
+    DeviceGuard guard(ctx->device);
+    const cudaIpcMemHandle_t* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+    cudaIpcMemHandle_t own;
+    OCL_CUDA(ctx, cudaIpcGetMemHandle(&own, c->buf), "tp_comm_open: own handle");
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        if (memcmp(&hs[p], &own, sizeof own) == 0) {  // loopback: a peer slot mapped onto this rank's buffer
+            c->peer[p] = c->buf;
+            continue;
+        }
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "tp_comm_open: cudaIpcOpenMemHandle");
+        c->peer[p] = ptr;
+    }
+    c->open = true;
+    return OCL_OK;
+}
+
+int ocl_tp_comm_destroy(ocl_tpcomm* c) {
+    if (!c) return OCL_OK;
+    DeviceGuard guard(c->device);
+    cudaDeviceSynchronize();
+    for (int p = 0; p < c->world; ++p)
+        if (p != c->rank && c->peer[p] && c->peer[p] != c->buf) cudaIpcCloseMemHandle(c->peer[p]);
+    if (c->buf) cudaFree(c->buf);
+    delete c;
+    return OCL_OK;
+}
+
+int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const float* x_dev, size_t rows,
+                           size_t in_features, size_t out_features, const float* bias_dev, float* y_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_linear_shapes(ctx, w, rows, in_features, out_features);
+    if (rc) return rc;
+    if (!c || !c->open) return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: communicator not opened");
+    if (c->device != ctx->device) return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: communicator on another device");
+    if (!x_dev || !y_dev) return fail(ctx, OCL_ERR_INVALID, "linear_allreduce x/out pointer is null");
+    DeviceGuard guard(ctx->device);
+    const size_t k = w->k, n = w->n_rows;
+    rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
+    if (rc) return rc;
+    const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
+    ocl::TpArgs tp;
+    tp.world = c->world;
+    tp.rank = c->rank;
+    tp.max_elems = c->max_elems;
+    tp.max_groups = c->max_groups;
+    for (int p = 0; p < c->world; ++p) {
+        tp.recv[p] = static_cast<float*>(c->peer[p]);
+        tp.flags[p] = reinterpret_cast<unsigned int*>(static_cast<char*>(c->peer[p]) +
+                                                      (size_t)2 * c->world * c->max_elems * 4);
+    }
+    tp.ctl = tp.flags[c->rank] + (size_t)c->world * c->max_groups;
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
+        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+        ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
+        if (!ocl::plan_single_split(pl, w->type, m))
+            return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `fused all-reduce shape` (requested `%zu x %zu`):"
+                        " supported = [activation planes of the full K within shared memory]", n, k);
+        if ((int64_t)m * (int64_t)n > c->max_elems || pl.groups > c->max_groups)
+            return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: %d x %zu outputs (%lld CTAs) exceed the communicator "
+                        "capacity (%lld elements, %lld groups)", m, n, (long long)pl.groups,
+                        (long long)c->max_elems, (long long)c->max_groups);
+        OCL_CUDA(ctx, ocl::launch_xsplit(x_dev + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream),
+                 "x split launch");
+        OCL_CUDA(ctx,
+                 ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias_dev, y_dev + r0 * n, pl,
+                                  ctx->part, ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream, &tp),
+                 "fused linear + all-reduce launch");
+    }
     return OCL_OK;
 }
 

@@ -532,6 +532,85 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
 // blockIdx.y = cross-CTA K split.  Warp w owns row tile (w % RT) and K slice
 // (w / RT) of the CTA's range.
 // ---------------------------------------------------------------------------
+// Fused tensor-parallel all-reduce of this CTA's rows (called instead of the
+// plain epilogue when a.tp.world > 1, ks == 1):
+//  1. push the rows (sum of the KW slices, no bias) into slot [rank] of every
+//     rank's receive buffer (P2P stores over NVLink; own buffer included);
+//  2. system fence, then set flag [rank][group] on every rank to epoch + 1;
+//  3. wait (bounded, ~1 s) until every rank's flag for this group arrived here;
+//  4. sum the world slots in rank order (+ bias): every rank gets the same bits.
+// The epoch lives in device memory (so CUDA-graph replays advance it); the last
+// CTA to finish bumps it, and its parity picks one of two data buffers, so a
+// rank one launch ahead never overwrites data a peer is still reading.
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, int RT, int KW, int64_t r0) {
+    __shared__ unsigned int ep_s;
+    __shared__ int failed_s;
+    const TpArgs& tp = a.tp;
+    if (threadIdx.x == 0) {
+        ep_s = *reinterpret_cast<volatile unsigned int*>(tp.ctl);
+        failed_s = 0;
+    }
+    __syncthreads();
+    const unsigned int ep = ep_s, tag = ep + 1u, par = ep & 1u;
+    const int64_t nrows = RT * 16;
+    for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
+        const int m = (int)(idx / nrows), rl = (int)(idx - (int64_t)m * nrows);
+        const int tile = rl >> 4, row = rl & 15;
+        const int64_t o = r0 + rl;
+        if (o >= a.n) continue;
+        float v = 0.f;
+        for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
+        const int64_t e = ((int64_t)(par * tp.world + tp.rank)) * tp.max_elems + (int64_t)m * a.n + o;
+        for (int p = 0; p < tp.world; ++p) tp.recv[p][e] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if ((int)threadIdx.x < tp.world)
+        st_release_sys(tp.flags[threadIdx.x] + (int64_t)tp.rank * tp.max_groups + blockIdx.x, tag);
+    if ((int)threadIdx.x < tp.world) {
+        const unsigned int* f = tp.flags[tp.rank] + (int64_t)threadIdx.x * tp.max_groups + blockIdx.x;
+        const long long t0 = clock64();
+        while (ld_acquire_sys(f) != tag) {
+            if (clock64() - t0 > 2000000000LL) {
+                atomicExch(&failed_s, 1);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (failed_s) {
+        if (threadIdx.x == 0) atomicAdd(a.err + 1, 1u);
+    } else {
+        const float* mine = tp.recv[tp.rank] + (int64_t)par * tp.world * tp.max_elems;
+        for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
+            const int m = (int)(idx / nrows);
+            const int64_t o = r0 + (idx - (int64_t)m * nrows);
+            if (o >= a.n) continue;
+            float v = 0.f;
+            for (int s2 = 0; s2 < tp.world; ++s2) v += __ldcg(mine + (int64_t)s2 * tp.max_elems + (int64_t)m * a.n + o);
+            a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+        }
+    }
+    // advance the epoch once every CTA of this launch is through
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(tp.ctl + 1, 1u) == gridDim.x * gridDim.y - 1) {
+            tp.ctl[1] = 0;
+            __threadfence();
+            atomicAdd(tp.ctl, 1u);
+        }
+    }
+}
+
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
@@ -695,6 +774,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 
     // 5. add the KW slices of each row tile in slice order; write y or a partial
     const int64_t r0 = (int64_t)blockIdx.x * RT * 16;
+    if (a.tp.world > 1) {  // row-split layer: sum over ranks through peer memory
+        tp_epilogue(a, red, RT, KW, r0);
+        return;
+    }
     for (int idx = threadIdx.x; idx < RT * 16 * a.rows; idx += blockDim.x) {
         const int m = idx / (RT * 16), rl = idx - m * RT * 16;
         const int tile = rl >> 4, row = rl & 15;
@@ -823,6 +906,14 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
     return pl;
 }
 
+bool plan_single_split(GemvPlan& pl, int type, int rows) {
+    pl.ks = 1;
+    pl.umax = pl.n_units;
+    pl.smem = (size_t)smem_map(type, pl.nt, pl.umax, rows).total;
+    pl.part_floats = 0;
+    return pl.smem <= 220 * 1024;
+}
+
 XPlanes xplanes_carve(void* base, int64_t k) {
     XPlanes p;
     p.kx = (int)((k + 255) / 256 * 256);
@@ -858,8 +949,12 @@ cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p,
 
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
-                        unsigned int* err, bool pdl, cudaStream_t s) {
+                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp) {
     GemvArgs a{};
+    if (tp) {
+        if (pl.ks != 1) return cudaErrorInvalidValue;
+        a.tp = *tp;
+    }
     a.W = (const uint8_t*)tiles;
     a.n = n;
     a.k = k;

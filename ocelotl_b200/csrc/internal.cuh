@@ -60,6 +60,26 @@ struct GemvPlan {
     size_t part_floats; // cross-CTA partial sums (0 when ks == 1)
 };
 GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms);
+// Same plan without a cross-CTA K split (required by the fused all-reduce);
+// false if the CTA's activation planes then no longer fit in shared memory.
+bool plan_single_split(GemvPlan& pl, int type, int rows);
+
+// Tensor-parallel all-reduce fused into the GEMV epilogue (row-split layers).
+// Every rank owns one buffer: data [2 parities][world][max_elems] f32, then
+// flags [world][max_groups] u32, then {epoch, done counter}; peers' buffers are
+// mapped into this process (CUDA IPC over NVLink), so recv[p] / flags[p] are
+// rank p's buffer as seen from here.
+constexpr int kTpMax = 8;
+struct TpArgs {
+    int world = 1, rank = 0;
+    int64_t max_elems = 0, max_groups = 0;
+    float* recv[kTpMax] = {};
+    unsigned int* flags[kTpMax] = {};
+    unsigned int* ctl = nullptr;  // local: [0] epoch, [1] CTAs done this launch
+};
+inline size_t tp_buffer_bytes(int world, int64_t max_elems, int64_t max_groups) {
+    return (size_t)2 * world * max_elems * 4 + (size_t)world * max_groups * 4 + 256;
+}
 
 struct GemvArgs {
     const uint8_t* W;
@@ -72,6 +92,7 @@ struct GemvArgs {
     float* part;             // [ks][rows][n] when ks > 1
     unsigned int* counters;  // [groups], zero between launches
     unsigned int* err;       // [0] bad embedding ids, [1] bounded waits that gave up
+    TpArgs tp;               // world > 1: sum the rows over ranks in the epilogue (ks must be 1)
 };
 
 // y [rows<=16, n] = planes . W^T (+ bias), geometry from plan_gemv.  `pdl`
@@ -79,7 +100,7 @@ struct GemvArgs {
 // predecessor before reading the planes).
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
-                        unsigned int* err, bool pdl, cudaStream_t s);
+                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp = nullptr);
 
 // Prefill GEMM: y bf16 [M, N] = x bf16 [M, K] . W^T on tcgen05 (K a multiple of 256).
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,

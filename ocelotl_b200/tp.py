@@ -44,6 +44,46 @@ def shard_in(blocks, ggml_type: int, n_rows: int, k: int, rank: int, world: int)
     return np.ascontiguousarray(b[:, kb0:kb1]).reshape(-1), kb0 * g.elems, kb1 * g.elems
 
 
+class TPComm:
+    """This rank's peer-memory buffers for the fused all-reduce (one per process and GPU).
+
+    Creates the receive buffer, exchanges CUDA IPC handles over `group` (any
+    torch.distributed backend; handles travel as bytes) and maps the peers'
+    buffers.  `handles` may be given instead of a group (all ranks' 64-byte
+    handles in rank order), e.g. for a loopback test.
+    """
+
+    def __init__(self, backend, rank: int, world: int, max_elems: int, max_groups: int = 4096,
+                 group=None, handles: list[bytes] | None = None):
+        import ctypes as C
+        self.backend = backend
+        self.rank, self.world = rank, world
+        h = C.c_void_p()
+        own = (C.c_char * 64)()
+        backend._check(backend._lib.ocl_tp_comm_create(backend._ctx, rank, world, max_elems, max_groups,
+                                                       C.byref(h), own))
+        self.handle = h
+        self.own_handle = bytes(own)
+        if handles is None:
+            import torch.distributed as dist
+            gathered = [None] * world
+            dist.all_gather_object(gathered, self.own_handle, group=group)
+            handles = gathered
+        buf = (C.c_char * (64 * world)).from_buffer_copy(b"".join(handles))
+        backend._check(backend._lib.ocl_tp_comm_open(backend._ctx, h, buf))
+
+    def close(self):
+        if self.handle:
+            self.backend._lib.ocl_tp_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class TPLinear:
     """One rank's shard of a quantized linear layer on its own GPU.
 
@@ -52,17 +92,21 @@ class TPLinear:
     """
 
     def __init__(self, backend, ggml_type: int, shard_blocks, n_local: int, k_local: int, mode: str,
-                 group=None):
+                 group=None, comm: TPComm | None = None):
         if mode not in ("out", "in"):
             raise ValueError(mode)
         self.backend = backend
         self.mode = mode
         self.group = group
+        self.comm = comm  # mode "in": fused peer-memory all-reduce instead of torch.distributed
         self.n, self.k = n_local, k_local
         self.weight = backend.upload_quant(ggml_type, shard_blocks, n_local, k_local)
 
     def forward(self, x_local, rows: int, out) -> None:
         """x_local: this rank's input ([rows, k] for "out", [rows, k_local] for "in"), out [rows, n]."""
+        if self.mode == "in" and self.comm is not None:
+            self.backend.linear_allreduce(self.comm, self.weight, x_local, rows, out)
+            return
         self.backend.linear_dev(self.weight, x_local, rows, out)
         if self.mode == "in":
             import torch.distributed as dist
