@@ -310,7 +310,7 @@ def run_ocelotl(args):
     from ocelotl_b200 import synth
     from ocelotl_b200.backend import CudaKernelBackend
     from ocelotl_b200.build import build
-    from ocelotl_b200.tp import TPLinear
+    from ocelotl_b200.tp import TPComm, TPLinear
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -331,13 +331,15 @@ def run_ocelotl(args):
     sh = {name: (t, n, k, sp) for name, t, n, k, sp in shards}
     rank_wbytes = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
     copies = max(2, -(-4 * L2_BYTES // rank_wbytes))
+    # row-split layers sum over ranks inside the GEMV (peer memory); NCCL with --nccl
+    comm = TPComm(be, rank, tp, max_elems=16 * HIDDEN) if (tp > 1 and not args.nccl) else None
     weights = []
     for c in range(copies):
         ws = {}
         for name, t, n, k, sp in shards:
             # this rank's shard, generated in place (same distribution as a sharded full weight)
             blocks = synth.quant_blocks(t, n, k, args.seed, f"{name}.r{rank}.c{c}", device=dev)
-            ws[name] = TPLinear(be, t, blocks, n, k, "out" if sp == "col" else "in")
+            ws[name] = TPLinear(be, t, blocks, n, k, "out" if sp == "col" else "in", comm=comm)
             del blocks
         weights.append(ws)
     torch.cuda.synchronize()
@@ -493,8 +495,9 @@ def run_ocelotl(args):
                              f"({copies * rank_wbytes / 1e6:.0f} MB per GPU, >= 4x the 126 MB L2)",
                        "alg_bytes_per_step": layer_alg_bytes(m),
                        "pct_of_8TBps": round(100 * gbs / 8000.0, 2),
-                       "step": "CUDA graph of 5 ocl_q_linear calls" + ("" if tp == 1 else
-                                                                          " + 2 NCCL all-reduces (o, down)")},
+                       "step": "CUDA graph of 5 ocl_q_linear calls" + ("" if tp == 1 else (
+                           " + 2 NCCL all-reduces (o, down)" if args.nccl else
+                           "; o and down sum over ranks inside the GEMV (ocl_q_linear_allreduce, NVLink peer memory)"))},
             "roofline": roofline,
             "projections": proj,
             "cpu_baseline": cpu,
@@ -537,6 +540,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0x0CE107)
     ap.add_argument("--sweep", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nccl", action="store_true", help="TP: NCCL all-reduce instead of the fused one")
     ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
     ap.add_argument("--stack", type=int, default=1, help="also time configs[3] (8B linear stack per token)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)

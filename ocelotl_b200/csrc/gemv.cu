@@ -536,7 +536,7 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
 // plain epilogue when a.tp.world > 1, ks == 1):
 //  1. push the rows (sum of the KW slices, no bias) into slot [rank] of every
 //     rank's receive buffer (P2P stores over NVLink; own buffer included);
-//  2. system fence, then set flag [rank][group] on every rank to epoch + 1;
+//  2. CTA barrier, then release-store flag [rank][group] = epoch + 1 on every rank;
 //  3. wait (bounded, ~1 s) until every rank's flag for this group arrived here;
 //  4. sum the world slots in rank order (+ bias): every rank gets the same bits.
 // The epoch lives in device memory (so CUDA-graph replays advance it); the last
@@ -571,7 +571,9 @@ __device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, in
         const int64_t e = ((int64_t)(par * tp.world + tp.rank)) * tp.max_elems + (int64_t)m * a.n + o;
         for (int p = 0; p < tp.world; ++p) tp.recv[p][e] = v;
     }
-    __threadfence_system();
+    // The CTA barrier orders every thread's pushes before the flag writers'
+    // system-scope release stores (release is cumulative), so only those
+    // threads pay for the system-scope ordering.
     __syncthreads();
     if ((int)threadIdx.x < tp.world)
         st_release_sys(tp.flags[threadIdx.x] + (int64_t)tp.rank * tp.max_groups + blockIdx.x, tag);
