@@ -303,6 +303,69 @@ def run_stack(be, args, torch, synth, dev):
     return res
 
 
+LAYER_70B = [  # hidden 8192, GQA kv 1024 (q 8192 + k 1024 + v 1024), ffn 28672
+    ("qkv", Q4_K, 10240, 8192, "col"),
+    ("o", Q4_K, 8192, 8192, "row"),
+    ("gate", Q4_K, 28672, 8192, "col"),
+    ("up", Q4_K, 28672, 8192, "col"),
+    ("down", Q6_K, 8192, 28672, "row"),
+]
+
+
+def run_tp70b(be, args, torch, synth, dev, rank, tp, comm):
+    """one Llama-3-70B-shaped layer's projections under tensor parallelism (per decode token)."""
+    from ocelotl_b200.tp import TPLinear
+    import torch.distributed as dist
+    shards = [(nm, t, n // tp, k, sp) if sp == "col" else (nm, t, n, k // tp, sp) for nm, t, n, k, sp in LAYER_70B]
+    per_gpu = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
+    copies = max(1, -(-4 * L2_BYTES // per_gpu))
+    layers = []
+    for c in range(copies):
+        layers.append({nm: TPLinear(be, t, synth.quant_blocks(t, n, k, args.seed, f"70b.{nm}.r{rank}.c{c}", device=dev),
+                                    n, k, "out" if sp == "col" else "in", comm=comm)
+                       for nm, t, n, k, sp in shards})
+    total = sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER_70B)
+    out = {"per_gpu_weight_bytes": per_gpu, "layer_weight_bytes": total, "copies": copies}
+    xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+    for m in (1, 16):
+        xs = {nm: synth.activations(m, k, args.seed, f"70b.x.{nm}.r{rank}", device=dev) for nm, t, n, k, _ in shards}
+        ys = {nm: torch.empty(m, n, device=dev) for nm, t, n, k, _ in shards}
+
+        def step(c, m=m, xs=xs, ys=ys):
+            for nm, t, n, k, sp in shards:
+                layers[c][nm].forward(xs[xin[nm]], m, ys[nm])
+        for c in range(copies):
+            step(c)
+        torch.cuda.synchronize()
+        if tp > 1:
+            dist.barrier()
+        gs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
+        for i in range(3):
+            gs[i % copies].replay()
+        torch.cuda.synchronize()
+        if tp > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 30
+        a.record()
+        for i in range(reps):
+            gs[i % copies].replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = 1e3 * a.elapsed_time(b) / reps
+        if tp > 1:
+            t_ = torch.tensor([us], device=dev)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            us = float(t_.item())
+        out[str(m)] = {"layer_us": round(us, 1), "GB/s": round(total / (us * 1e-6) / 1e9, 1),
+                       "tok_s_80_layers": round(m / (80 * us * 1e-6), 1),
+                       "roofline_us_per_gpu": round(per_gpu / (6538.0e9) * 1e6, 1)}
+        del gs
+    del layers
+    torch.cuda.synchronize()
+    return out
+
+
 def run_ocelotl(args):
     import torch
     import torch.distributed as dist
@@ -332,7 +395,7 @@ def run_ocelotl(args):
     rank_wbytes = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
     copies = max(2, -(-4 * L2_BYTES // rank_wbytes))
     # row-split layers sum over ranks inside the GEMV (peer memory); NCCL with --nccl
-    comm = TPComm(be, rank, tp, max_elems=16 * HIDDEN) if (tp > 1 and not args.nccl) else None
+    comm = TPComm(be, rank, tp, max_elems=16 * 8192) if (tp > 1 and not args.nccl) else None
     weights = []
     for c in range(copies):
         ws = {}
@@ -477,6 +540,7 @@ def run_ocelotl(args):
                               "tok_s_layer": round(mm / (us * 1e-6), 1)}
             del gs
 
+    tp70 = run_tp70b(be, args, torch, synth, dev, rank, tp, comm) if args.tp70b else None
     prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
     stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
     errs = be.take_device_errors()
@@ -515,6 +579,8 @@ def run_ocelotl(args):
             line["m_sweep"] = sweep
         if prefill:
             line["prefill_gemm"] = prefill
+        if tp70:
+            line["tp_70b_layer"] = tp70
         if stack:
             line["linear_stack_8b"] = stack
         print(json.dumps(line), flush=True)
@@ -541,6 +607,7 @@ def main():
     ap.add_argument("--sweep", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="TP: NCCL all-reduce instead of the fused one")
+    ap.add_argument("--tp70b", type=int, default=1, help="also time configs[4] (70B-shaped layer, TP = N)")
     ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
     ap.add_argument("--stack", type=int, default=1, help="also time configs[3] (8B linear stack per token)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)

@@ -99,14 +99,21 @@ class TPLinear:
         self.mode = mode
         self.group = group
         self.comm = comm  # mode "in": fused peer-memory all-reduce instead of torch.distributed
+        self.fused: dict[int, bool] = {}  # rows -> whether the fused path applies
         self.n, self.k = n_local, k_local
         self.weight = backend.upload_quant(ggml_type, shard_blocks, n_local, k_local)
 
     def forward(self, x_local, rows: int, out) -> None:
         """x_local: this rank's input ([rows, k] for "out", [rows, k_local] for "in"), out [rows, n]."""
-        if self.mode == "in" and self.comm is not None:
-            self.backend.linear_allreduce(self.comm, self.weight, x_local, rows, out)
-            return
+        if self.mode == "in" and self.comm is not None and self.fused.get(rows, True):
+            try:
+                self.backend.linear_allreduce(self.comm, self.weight, x_local, rows, out)
+                self.fused[rows] = True
+                return
+            except UnsupportedError:
+                # shapes whose activation planes do not fit one CTA (e.g. K >= 4096
+                # at 16 rows): local GEMV + torch.distributed all-reduce instead
+                self.fused[rows] = False
         self.backend.linear_dev(self.weight, x_local, rows, out)
         if self.mode == "in":
             import torch.distributed as dist
