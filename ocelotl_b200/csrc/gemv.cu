@@ -550,7 +550,7 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, int RT, int KW, int64_t r0) {
+__device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red, int RT, int KW, int64_t r0) {
     __shared__ unsigned int ep_s;
     __shared__ int failed_s;
     const TpArgs& tp = a.tp;
@@ -569,16 +569,28 @@ __device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, in
         float v = 0.f;
         for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
         const int64_t e = ((int64_t)(par * tp.world + tp.rank)) * tp.max_elems + (int64_t)m * a.n + o;
-        for (int p = 0; p < tp.world; ++p) tp.recv[p][e] = v;
+#pragma unroll
+        for (int p = 0; p < kTpMax; ++p)  // constant indices keep the pointer table in parameter space
+            if (p < tp.world) tp.recv[p][e] = v;
     }
     // The CTA barrier orders every thread's pushes before the flag writers'
     // system-scope release stores (release is cumulative), so only those
     // threads pay for the system-scope ordering.
     __syncthreads();
-    if ((int)threadIdx.x < tp.world)
-        st_release_sys(tp.flags[threadIdx.x] + (int64_t)tp.rank * tp.max_groups + blockIdx.x, tag);
+#pragma unroll
+    for (int p = 0; p < kTpMax; ++p)
+        if (p < tp.world && (int)threadIdx.x == p)
+            st_release_sys(tp.flags[p] + (int64_t)tp.rank * tp.max_groups + blockIdx.x, tag);
+    const unsigned int* my_flags = nullptr;
+    const float* my_recv = nullptr;
+#pragma unroll
+    for (int p = 0; p < kTpMax; ++p)
+        if (p == tp.rank) {
+            my_flags = tp.flags[p];
+            my_recv = tp.recv[p];
+        }
     if ((int)threadIdx.x < tp.world) {
-        const unsigned int* f = tp.flags[tp.rank] + (int64_t)threadIdx.x * tp.max_groups + blockIdx.x;
+        const unsigned int* f = my_flags + (int64_t)threadIdx.x * tp.max_groups + blockIdx.x;
         const long long t0 = clock64();
         while (ld_acquire_sys(f) != tag) {
             if (clock64() - t0 > 2000000000LL) {
@@ -591,7 +603,7 @@ __device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, in
     if (failed_s) {
         if (threadIdx.x == 0) atomicAdd(a.err + 1, 1u);
     } else {
-        const float* mine = tp.recv[tp.rank] + (int64_t)par * tp.world * tp.max_elems;
+        const float* mine = my_recv + (int64_t)par * tp.world * tp.max_elems;
         for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
             const int m = (int)(idx / nrows);
             const int64_t o = r0 + (idx - (int64_t)m * nrows);
@@ -613,7 +625,7 @@ __device__ __noinline__ void tp_epilogue(const GemvArgs& a, const float* red, in
     }
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, bool TPF>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
     constexpr int UB = unit_bytes(TYPE), S = kStages, NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
@@ -776,7 +788,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 
     // 5. add the KW slices of each row tile in slice order; write y or a partial
     const int64_t r0 = (int64_t)blockIdx.x * RT * 16;
-    if (a.tp.world > 1) {  // row-split layer: sum over ranks through peer memory
+    if constexpr (TPF) {  // row-split layer: sum over ranks through peer memory
         tp_epilogue(a, red, RT, KW, r0);
         return;
     }
@@ -811,11 +823,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, bool TPF>
 cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
     static size_t configured = 0;  // per template instance: largest dynamic smem enabled so far
     if (pl.smem > 48 * 1024 && pl.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, TPF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)pl.smem);
         if (e != cudaSuccess) return e;
         configured = pl.smem;
@@ -830,21 +842,26 @@ cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT>, a);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT, TPF>, a);
+}
+
+template <int TYPE, bool TPF>
+cudaError_t launch_nt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
+    switch (pl.nt) {
+        case 0: return launch_typed<TYPE, 0, TPF>(pl, a, pdl, s);
+        case 1: return launch_typed<TYPE, 1, TPF>(pl, a, pdl, s);
+        case 2: return launch_typed<TYPE, 2, TPF>(pl, a, pdl, s);
+        case 3: return launch_typed<TYPE, 3, TPF>(pl, a, pdl, s);
+        case 4: return launch_typed<TYPE, 4, TPF>(pl, a, pdl, s);
+        case 5: return launch_typed<TYPE, 5, TPF>(pl, a, pdl, s);
+        case 6: return launch_typed<TYPE, 6, TPF>(pl, a, pdl, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <int TYPE>
-cudaError_t launch_nt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
-    switch (pl.nt) {
-        case 0: return launch_typed<TYPE, 0>(pl, a, pdl, s);
-        case 1: return launch_typed<TYPE, 1>(pl, a, pdl, s);
-        case 2: return launch_typed<TYPE, 2>(pl, a, pdl, s);
-        case 3: return launch_typed<TYPE, 3>(pl, a, pdl, s);
-        case 4: return launch_typed<TYPE, 4>(pl, a, pdl, s);
-        case 5: return launch_typed<TYPE, 5>(pl, a, pdl, s);
-        case 6: return launch_typed<TYPE, 6>(pl, a, pdl, s);
-        default: return cudaErrorInvalidValue;
-    }
+cudaError_t launch_tp(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
+    return a.tp.world > 1 ? launch_nt<TYPE, true>(pl, a, pdl, s) : launch_nt<TYPE, false>(pl, a, pdl, s);
 }
 
 }  // namespace
@@ -973,9 +990,9 @@ cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const
     a.part = part;
     a.counters = counters;
     a.err = err;
-    if (type == kQ4_K) return launch_nt<kQ4_K>(pl, a, pdl, s);
-    if (type == kQ6_K) return launch_nt<kQ6_K>(pl, a, pdl, s);
-    return launch_nt<kQ8_0>(pl, a, pdl, s);
+    if (type == kQ4_K) return launch_tp<kQ4_K>(pl, a, pdl, s);
+    if (type == kQ6_K) return launch_tp<kQ6_K>(pl, a, pdl, s);
+    return launch_tp<kQ8_0>(pl, a, pdl, s);
 }
 
 }  // namespace ocl
