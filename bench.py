@@ -366,6 +366,51 @@ def run_tp70b(be, args, torch, synth, dev, rank, tp, comm):
     return out
 
 
+def time_graphs(gs, n_it, torch):
+    for i in range(3):
+        gs[i % len(gs)].replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n_it):
+        gs[i % len(gs)].replay()
+    b.record()
+    torch.cuda.synchronize()
+    return 1e3 * a.elapsed_time(b) / n_it
+
+
+def run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev):
+    """The same layer with gate and up as one gated pass over an interleaved
+    pair (one GEMV launch streaming both, act = silu(gate) * up)."""
+    pairs = [be.pair_gated(weights[c]["gate"].weight, weights[c]["up"].weight) for c in range(copies)]
+    n_ffn = sh["gate"][1]
+    act = torch.empty(m, n_ffn, device=dev)
+    ys = {nm: torch.empty(m, sh[nm][1], device=dev) for nm in ("qkv", "o", "down")}
+
+    def step(c):
+        w = weights[c]
+        be.linear_dev(w["qkv"].weight, xs["qkv"], m, ys["qkv"])
+        be.linear_dev(w["o"].weight, xs["o"], m, ys["o"])
+        be.linear_gated(pairs[c], xs["gate"], m, act)
+        be.linear_dev(w["down"].weight, xs["down"], m, ys["down"])
+    gs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
+    us = time_graphs(gs, max(20, args.steps), torch)
+    reps = 2 * copies
+    g1 = graph_of(lambda: [be.linear_gated(pairs[r % copies], xs["gate"], m, act) for r in range(reps)], be, torch)
+    us_gu = time_graphs([g1], max(3, args.steps // 20), torch) / reps
+    t, n, k, _ = sh["gate"]
+    gu_bytes = 2 * wbytes(t, n, k) + 4 * m * k + 4 * m * n
+    del gs, g1
+    for p in pairs:
+        p.quant.free()
+    return {"layer_us": round(us, 3), "GB/s": round(layer_alg_bytes(m) / (us * 1e-6) / 1e9, 1),
+            "decode_tok_s_layer": round(m / (us * 1e-6), 1),
+            "gate_up_us": round(us_gu, 3), "gate_up_GB/s": round(gu_bytes / (us_gu * 1e-6) / 1e9, 1),
+            "gpu_launches_per_step": KERNELS_PER_CALL * 4,
+            "note": "qkv, o, gated(gate+up -> silu(gate)*up), down; GB/s over the same algorithmic bytes as the "
+                    "5-projection layer"}
+
+
 def run_ocelotl(args):
     import torch
     import torch.distributed as dist
@@ -540,6 +585,8 @@ def run_ocelotl(args):
                               "tok_s_layer": round(mm / (us * 1e-6), 1)}
             del gs
 
+    fused = run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev) if (args.fused_mlp and tp == 1) \
+        else None
     tp70 = run_tp70b(be, args, torch, synth, dev, rank, tp, comm) if args.tp70b else None
     prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
     stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
@@ -579,6 +626,8 @@ def run_ocelotl(args):
             line["m_sweep"] = sweep
         if prefill:
             line["prefill_gemm"] = prefill
+        if fused:
+            line["layer_fused_mlp"] = fused
         if tp70:
             line["tp_70b_layer"] = tp70
         if stack:
@@ -610,6 +659,8 @@ def main():
     ap.add_argument("--tp70b", type=int, default=1, help="also time configs[4] (70B-shaped layer, TP = N)")
     ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
     ap.add_argument("--stack", type=int, default=1, help="also time configs[3] (8B linear stack per token)")
+    ap.add_argument("--fused-mlp", type=int, default=1,
+                    help="also time the layer with gate+up as one fused gated pass (ocl_q_linear_gated)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -190,6 +190,37 @@ OCL_API int ocl_q_linear_noalloc(int ggml_type, const void* w_tiled_dev, size_t 
 OCL_API int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_dev, size_t rows,
                     size_t in_features, size_t out_features, uint16_t* y_dev);
 
+/* Fused gated MLP (crates/kernels/src/mlp.rs:139-240, KernelBackend::mlp_gated_silu
+ * at crates/kernels/src/lib.rs:150).  The reference multiplies by f32 gate_w /
+ * up_w [hidden, intermediate] and down_w [intermediate, hidden]; here they are
+ * GGUF quantized weights, GGUF-shaped (rows = out features, k = in features).
+ *
+ * ocl_q_pair_gated: a new buffer holding gate and up (same type and shape) as
+ * interleaved 16-row tiles, so one GEMV pass streams both against one copy of
+ * x.  The inputs stay valid and owned by the caller; free the pair with
+ * ocl_q_free.  A pair is accepted only by the gated calls below.
+ *
+ * ocl_q_linear_gated: act f32 [rows, intermediate] = silu(x . gate^T) * (x . up^T),
+ * silu(z) = z / (1 + exp(-z)), in one launch over the pair.
+ *
+ * ocl_q_mlp_gated_silu: out f32 [rows, hidden] = act . down^T after
+ * ocl_q_linear_gated; act_dev is the caller's [rows, intermediate] scratch (the
+ * reference's gate_buf, which likewise ends holding silu(gate) * up).  Errors
+ * follow the reference's checks: zero seq_len / hidden / intermediate and shape
+ * mismatches are OCL_ERR_INVALID.  Tolerance as ocl_q_linear per projection.
+ *
+ * ocl_q_gemm_gated_bf16: prefill form, act bf16 [rows, intermediate] for bf16 x
+ * [rows, hidden] (hidden a multiple of 256, x 16-byte aligned): one tcgen05
+ * GEMM over the pair, silu * up applied to the f32 accumulators before the
+ * bf16 store. */
+OCL_API int ocl_q_pair_gated(ocl_ctx* ctx, const ocl_qbuf* gate, const ocl_qbuf* up, ocl_qbuf** out);
+OCL_API int ocl_q_linear_gated(ocl_ctx* ctx, const ocl_qbuf* gate_up, const float* x_dev, size_t rows,
+                               size_t hidden, size_t intermediate, float* act_dev);
+OCL_API int ocl_q_mlp_gated_silu(ocl_ctx* ctx, const ocl_qbuf* gate_up, const ocl_qbuf* down, const float* x_dev,
+                                 size_t rows, size_t hidden, size_t intermediate, float* act_dev, float* out_dev);
+OCL_API int ocl_q_gemm_gated_bf16(ocl_ctx* ctx, const ocl_qbuf* gate_up, const uint16_t* x_dev, size_t rows,
+                                  size_t hidden, size_t intermediate, uint16_t* act_dev);
+
 /* Q8_0 embedding gather: out f32 [n_ids, k] = dequantized rows ids[i] of `table`
  * (ids int32 in device memory), bit-exact with the GGUF block arithmetic.  The
  * ids are only known on the device, so an id outside [0, n_rows) cannot fail the

@@ -42,19 +42,21 @@ class QuantBuffer:
     unsupported for quantized buffers.
     """
 
-    def __init__(self, backend: "CudaKernelBackend", handle: int, ggml_type: int, n_rows: int, k: int):
+    def __init__(self, backend: "CudaKernelBackend", handle: int, ggml_type: int, n_rows: int, k: int,
+                 gated: bool = False):
         self._backend = backend
         self._handle = C.c_void_p(handle)
         self.ggml_type = GgmlType(ggml_type)
         self.n_rows = n_rows
         self.k = k
+        self.gated = gated  # interleaved gate/up pair (n_rows each); only the gated-MLP calls take it
 
     # DeviceBuffer surface -------------------------------------------------
     def backend_id(self) -> str:
         return BACKEND_ID
 
     def len_f32(self) -> int:
-        return self.n_rows * self.k
+        return (2 if self.gated else 1) * self.n_rows * self.k
 
     def to_host(self) -> np.ndarray:
         return self._backend.dequant(self).cpu().numpy().reshape(-1)
@@ -328,3 +330,88 @@ class CudaKernelBackend:
         self._check(self._lib.ocl_q_linear(self._ctx, w.handle, C.c_void_p(x.data_ptr()), rows, w.k, w.n_rows,
                                            C.c_void_p(bias.data_ptr()) if bias is not None else None,
                                            C.c_void_p(out.data_ptr())))
+
+    # -- fused gated MLP (crates/kernels/src/mlp.rs:139-240) ---------------------
+    def pair_gated(self, gate, up) -> DeviceTensor:
+        """Interleave a gate and an up weight (same type and shape) into one pair buffer."""
+        g, u = self._quant_weight(gate), self._quant_weight(up)
+        h = C.c_void_p()
+        self._check(self._lib.ocl_q_pair_gated(self._ctx, g.handle, u.handle, C.byref(h)))
+        return DeviceTensor(quant=QuantBuffer(self, h.value, g.ggml_type, g.n_rows, g.k, gated=True))
+
+    def linear_gated(self, gate_up, x: torch.Tensor, rows: int, act: torch.Tensor) -> None:
+        """act [rows, intermediate] = silu(x . gate^T) * (x . up^T), one pass over the pair."""
+        w = self._quant_weight(gate_up)
+        self._check(self._lib.ocl_q_linear_gated(self._ctx, w.handle, C.c_void_p(x.data_ptr()), rows, w.k,
+                                                 w.n_rows, C.c_void_p(act.data_ptr())))
+
+    def gemm_gated_bf16(self, gate_up, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Prefill: bf16 [rows, hidden] -> bf16 silu(x . gate^T) * (x . up^T) on tcgen05 tensor cores."""
+        w = self._quant_weight(gate_up)
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous() or x.device != self.torch_device:
+            raise _kernel_err("gemm_gated_bf16 x must be a contiguous 2-D bf16 tensor on " + str(self.torch_device))
+        rows = x.shape[0]
+        if out is None:
+            out = torch.empty(rows, w.n_rows, dtype=torch.bfloat16, device=self.torch_device)
+        if tuple(out.shape) != (rows, w.n_rows) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise _kernel_err(f"gemm_gated_bf16 out must be a contiguous bf16 [{rows}, {w.n_rows}] tensor")
+        self._check(self._lib.ocl_q_gemm_gated_bf16(self._ctx, w.handle, C.c_void_p(x.data_ptr()), rows, x.shape[1],
+                                                    w.n_rows, C.c_void_p(out.data_ptr())))
+        return out
+
+    def mlp_gated_silu(self, x, rows: int, hidden: int, intermediate: int, gate_w, up_w, down_w,
+                       gate_buf, up_buf, out) -> None:
+        """KernelBackend::mlp_gated_silu (crates/kernels/src/lib.rs:150) on quantized weights.
+
+        gate_w is either a pair from `pair_gated` (then up_w is None) or a plain
+        gate weight with up_w its partner, paired for this call only.  x / gate_buf
+        / out are either contiguous f32 tensors on this device or host f32 numpy
+        arrays (then copied in and out).  gate_buf ends holding silu(gate) * up,
+        as in the reference; up_buf is accepted for signature parity and left
+        untouched (the fused pass never materialises up).
+        """
+        if rows == 0:
+            raise _kernel_err("mlp_gated_silu seq_len must be non-zero")
+        if hidden == 0:
+            raise _kernel_err("mlp_gated_silu hidden must be non-zero")
+        if intermediate == 0:
+            raise _kernel_err("mlp_gated_silu intermediate must be non-zero")
+        temp = None
+        gw = self._quant_weight(gate_w)
+        if not gw.gated:
+            if up_w is None:
+                raise _kernel_err("mlp_gated_silu up_w is required unless gate_w is a gate/up pair")
+            temp = self.pair_gated(gw, up_w)
+            gw = temp.quant
+        elif up_w is not None and self._quant_weight(up_w) is not gw:
+            raise _kernel_err("mlp_gated_silu gate_w is already a gate/up pair; pass up_w=None")
+        dw = self._quant_weight(down_w)
+        host = not isinstance(x, torch.Tensor)
+        sizes = {"x": rows * hidden, "gate_buf": rows * intermediate, "out": rows * hidden}
+        for name, t in (("x", x), ("gate_buf", gate_buf), ("out", out)):
+            n = t.numel() if isinstance(t, torch.Tensor) else np.asarray(t).size
+            if n != sizes[name]:
+                raise _kernel_err(f"mlp_gated_silu {name} length {n} does not match {sizes[name]}")
+        try:
+            if host:
+                xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32).reshape(-1)).to(self.torch_device)
+                ad = torch.empty(rows * intermediate, dtype=torch.float32, device=self.torch_device)
+                od = torch.empty(rows * hidden, dtype=torch.float32, device=self.torch_device)
+                torch.cuda.synchronize(self.torch_device)  # the copy-in ran on torch's stream
+            else:
+                xd, ad, od = x, gate_buf, out
+                for t in (xd, ad, od):
+                    if t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.torch_device:
+                        raise _kernel_err("mlp_gated_silu operands must be contiguous f32 tensors on "
+                                          + str(self.torch_device))
+            self._check(self._lib.ocl_q_mlp_gated_silu(
+                self._ctx, gw.handle, dw.handle, C.c_void_p(xd.data_ptr()), rows, hidden, intermediate,
+                C.c_void_p(ad.data_ptr()), C.c_void_p(od.data_ptr())))
+            if host:
+                self.synchronize()
+                np.copyto(gate_buf.reshape(-1), ad.cpu().numpy())
+                np.copyto(out.reshape(-1), od.cpu().numpy())
+        finally:
+            if temp is not None:
+                self.synchronize()
+                temp.quant.free()

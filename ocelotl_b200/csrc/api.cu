@@ -43,6 +43,7 @@ struct ocl_qbuf {
     int type = 0;
     size_t n_rows = 0, k = 0, bytes = 0;
     void* dev = nullptr;
+    bool gated = false;  // interleaved gate/up row tiles; n_rows = gate (= up) rows
 };
 
 namespace {
@@ -149,6 +150,8 @@ int ensure_split_buffers(ocl_ctx* ctx, const ocl::GemvPlan& pl) {
 
 int check_linear_shapes(ocl_ctx* ctx, const ocl_qbuf* w, size_t rows, size_t in_features, size_t out_features) {
     if (!w) return fail(ctx, OCL_ERR_INVALID, "linear_d weight is null");
+    if (w->gated)
+        return fail(ctx, OCL_ERR_INVALID, "linear_d weight is a gate/up pair; use ocl_q_linear_gated / ocl_q_mlp_gated_silu");
     if (w->device != ctx->device)
         return fail(ctx, OCL_ERR_INVALID, "weight lives on device %d but the context is on device %d", w->device,
                     ctx->device);
@@ -179,6 +182,44 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
                                   ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
                  "gemv launch");
     }
+    return OCL_OK;
+}
+
+// act [rows, n_gate] = silu(x . Wg^T) * (x . Wu^T) over an interleaved pair.
+int q_gated_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, float* act) {
+    const size_t k = w->k, n = w->n_rows;
+    int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
+    if (rc) return rc;
+    ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
+        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+        const ocl::GemvPlan pl = ocl::plan_gemv_gated(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
+        rc = ensure_split_buffers(ctx, pl);
+        if (rc) return rc;
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream), "x split launch");
+        OCL_CUDA(ctx,
+                 ocl::launch_gemv_gated(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, act + r0 * n, pl,
+                                        ctx->part, ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
+                 "gated gemv launch");
+    }
+    return OCL_OK;
+}
+
+int check_gated_shapes(ocl_ctx* ctx, const ocl_qbuf* gu, size_t rows, size_t hidden, size_t intermediate) {
+    if (!gu) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu gate/up weight is null");
+    if (!gu->gated) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu weight is not a gate/up pair (ocl_q_pair_gated)");
+    if (gu->device != ctx->device)
+        return fail(ctx, OCL_ERR_INVALID, "weight lives on device %d but the context is on device %d", gu->device,
+                    ctx->device);
+    if (rows == 0) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu seq_len must be non-zero");
+    if (hidden == 0) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu hidden must be non-zero");
+    if (intermediate == 0) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu intermediate must be non-zero");
+    if (gu->k != hidden)
+        return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu gate_w in_features=%zu does not match hidden=%zu", gu->k,
+                    hidden);
+    if (gu->n_rows != intermediate)
+        return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu gate_w out_features=%zu does not match intermediate=%zu",
+                    gu->n_rows, intermediate);
     return OCL_OK;
 }
 
@@ -333,6 +374,7 @@ int ocl_q_dequant(ocl_ctx* ctx, const ocl_qbuf* w, float* out_dev) {
     if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
     if (!w || !out_dev) return fail(ctx, OCL_ERR_INVALID, "ocl_q_dequant: null argument");
+    if (w->gated) return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `dequant of a gate/up pair`");
     DeviceGuard guard(ctx->device);
     OCL_CUDA(ctx, ocl::launch_dequant(w->type, w->dev, (int64_t)w->n_rows, (int64_t)w->k, out_dev, ctx->stream),
              "dequant launch");
@@ -343,6 +385,7 @@ int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_blocks) {
     if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
     if (!w || !host_blocks) return fail(ctx, OCL_ERR_INVALID, "ocl_q_download_gguf: null argument");
+    if (w->gated) return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `download of a gate/up pair`");
     DeviceGuard guard(ctx->device);
     const size_t bytes = w->n_rows * (w->k / (size_t)ocl::block_elems(w->type)) * (size_t)ocl::block_bytes(w->type);
     void* tmp = nullptr;
@@ -532,6 +575,83 @@ int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const
     return OCL_OK;
 }
 
+int ocl_q_pair_gated(ocl_ctx* ctx, const ocl_qbuf* gate, const ocl_qbuf* up, ocl_qbuf** out) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!out) return fail(ctx, OCL_ERR_INVALID, "ocl_q_pair_gated: out is null");
+    *out = nullptr;
+    if (!gate || !up) return fail(ctx, OCL_ERR_INVALID, "ocl_q_pair_gated: null weight");
+    if (gate->gated || up->gated) return fail(ctx, OCL_ERR_INVALID, "ocl_q_pair_gated: input is already a pair");
+    if (gate->type != up->type)
+        return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `gate/up of different types` (requested `%s/%s`)",
+                    type_name(gate->type), type_name(up->type));
+    if (gate->n_rows != up->n_rows || gate->k != up->k)
+        return fail(ctx, OCL_ERR_INVALID, "gate [%zu x %zu] and up [%zu x %zu] shapes differ", gate->n_rows, gate->k,
+                    up->n_rows, up->k);
+    if (gate->device != ctx->device || up->device != ctx->device)
+        return fail(ctx, OCL_ERR_INVALID, "gate/up weights are not on the context's device %d", ctx->device);
+    DeviceGuard guard(ctx->device);
+    const size_t n_rt = (gate->n_rows + 15) / 16, tile = gate->bytes / n_rt;
+    ocl_qbuf* w = new ocl_qbuf();
+    w->device = ctx->device;
+    w->type = gate->type;
+    w->n_rows = gate->n_rows;
+    w->k = gate->k;
+    w->bytes = 2 * gate->bytes;
+    w->gated = true;
+    cudaError_t e = cudaMalloc(&w->dev, w->bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail(ctx, e, "cudaMalloc(gate/up pair)");
+    }
+    // row tile t of gate -> tile 2t, of up -> tile 2t+1
+    e = cudaMemcpy2DAsync(w->dev, 2 * tile, gate->dev, tile, tile, n_rt, cudaMemcpyDeviceToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync((char*)w->dev + tile, 2 * tile, up->dev, tile, tile, n_rt, cudaMemcpyDeviceToDevice,
+                              ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFree(w->dev);
+        delete w;
+        return cuda_fail(ctx, e, "gate/up interleave");
+    }
+    *out = w;
+    return OCL_OK;
+}
+
+int ocl_q_linear_gated(ocl_ctx* ctx, const ocl_qbuf* gate_up, const float* x_dev, size_t rows, size_t hidden,
+                       size_t intermediate, float* act_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_gated_shapes(ctx, gate_up, rows, hidden, intermediate);
+    if (rc) return rc;
+    if (!x_dev || !act_dev) return fail(ctx, OCL_ERR_INVALID, "linear_gated x/act pointer is null");
+    DeviceGuard guard(ctx->device);
+    return q_gated_locked(ctx, gate_up, x_dev, rows, act_dev);
+}
+
+int ocl_q_mlp_gated_silu(ocl_ctx* ctx, const ocl_qbuf* gate_up, const ocl_qbuf* down, const float* x_dev, size_t rows,
+                         size_t hidden, size_t intermediate, float* act_dev, float* out_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_gated_shapes(ctx, gate_up, rows, hidden, intermediate);
+    if (rc) return rc;
+    if (!down) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu down_w is null");
+    if (down->gated) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu down_w is a gate/up pair");
+    if (down->device != ctx->device)
+        return fail(ctx, OCL_ERR_INVALID, "down_w lives on device %d but the context is on device %d", down->device,
+                    ctx->device);
+    if (down->k != intermediate || down->n_rows != hidden)
+        return fail(ctx, OCL_ERR_INVALID,
+                    "mlp_gated_silu down_w [%zu x %zu] does not match shape %zux%zu (out x in)", down->n_rows, down->k,
+                    hidden, intermediate);
+    if (!x_dev || !act_dev || !out_dev) return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu x/act/out pointer is null");
+    DeviceGuard guard(ctx->device);
+    rc = q_gated_locked(ctx, gate_up, x_dev, rows, act_dev);
+    if (rc) return rc;
+    return q_linear_locked(ctx, down, act_dev, rows, nullptr, out_dev);
+}
+
 int ocl_set_pdl(ocl_ctx* ctx, int enable) {
     if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);
@@ -557,6 +677,27 @@ int ocl_q_gemm_bf16(ocl_ctx* ctx, const ocl_qbuf* w, const uint16_t* x_dev, size
              ocl::launch_qgemm(w->type, w->dev, (int64_t)rows, (int64_t)out_features, (int64_t)in_features, x_dev,
                                y_dev, ctx->dev_flags, ctx->stream),
              "q_gemm launch");
+    return OCL_OK;
+}
+
+int ocl_q_gemm_gated_bf16(ocl_ctx* ctx, const ocl_qbuf* gate_up, const uint16_t* x_dev, size_t rows, size_t hidden,
+                          size_t intermediate, uint16_t* act_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int rc = check_gated_shapes(ctx, gate_up, rows, hidden, intermediate);
+    if (rc) return rc;
+    if (hidden % 256 != 0)
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `q_gemm_gated_bf16 hidden` (requested `%zu`): supported = [multiples of 256]",
+                    hidden);
+    if (!x_dev || !act_dev) return fail(ctx, OCL_ERR_INVALID, "q_gemm_gated_bf16 x/act pointer is null");
+    if (((uintptr_t)x_dev & 15) != 0) return fail(ctx, OCL_ERR_INVALID, "q_gemm_gated_bf16 x must be 16-byte aligned");
+    DeviceGuard guard(ctx->device);
+    const int64_t n_int = (int64_t)((intermediate + 15) / 16) * 32;
+    OCL_CUDA(ctx,
+             ocl::launch_qgemm(gate_up->type, gate_up->dev, (int64_t)rows, n_int, (int64_t)hidden, x_dev, act_dev,
+                               ctx->dev_flags, ctx->stream, (int64_t)intermediate),
+             "q_gemm_gated launch");
     return OCL_OK;
 }
 

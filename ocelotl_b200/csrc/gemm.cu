@@ -35,6 +35,8 @@ constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;  // 32 KB + 16 KB pe
 constexpr int PRODUCER_WARPS = 8, TMA_WARP = 8, MMA_WARP = 9, THREADS = 320;
 constexpr long long kWaitCycles = 2000000000LL;
 
+// silu(z) * u, silu(z) = z * (1 / (1 + exp(-z))) (crates/kernels/src/mlp.rs:77-86)
+__device__ __forceinline__ float silu_mul(float z, float u) { return z * (1.0f / (1.0f + expf(-z))) * u; }
 __device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mb_init(uint64_t* b, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(n));
@@ -253,10 +255,14 @@ __device__ __forceinline__ void dequant_quarter(const UnitRegs& R, int qt, int r
     }
 }
 
-template <int TYPE>
+// GATED: W holds interleaved gate/up row tiles (tile 2t = gate tile t, tile
+// 2t+1 = up tile t; N = their total padded rows) and y [M, n_out] =
+// silu(gate) * up: each 32-column accumulator slice a thread reads is one
+// (gate, up) pair of 16-row tiles.
+template <int TYPE, bool GATED>
 __global__ void __launch_bounds__(THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, int64_t M, int64_t N,
-                 int64_t K, uint16_t* __restrict__ y, unsigned int* __restrict__ err) {
+                 int64_t K, uint16_t* __restrict__ y, int64_t n_out, unsigned int* __restrict__ err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -383,7 +389,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                       "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
                     : "r"(taddr));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (m < M) {
+                if (m < M && GATED) {
+                    uint32_t p[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        p[i] = pack_bf16(silu_mul(__uint_as_float(v[2 * i]), __uint_as_float(v[16 + 2 * i])),
+                                         silu_mul(__uint_as_float(v[2 * i + 1]), __uint_as_float(v[17 + 2 * i])));
+                    const int64_t n = (n0 + c0) / 2;
+                    uint16_t* dst = y + m * n_out + n;
+                    if (n + 16 <= n_out && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+                        reinterpret_cast<uint4*>(dst)[0] = make_uint4(p[0], p[1], p[2], p[3]);
+                        reinterpret_cast<uint4*>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
+                    } else {
+                        for (int i = 0; i < 16 && n + i < n_out; ++i)
+                            dst[i] = (uint16_t)(i & 1 ? p[i >> 1] >> 16 : p[i >> 1] & 0xffffu);
+                    }
+                } else if (m < M) {
                     uint32_t p[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) p[i] = pack_bf16(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
@@ -427,25 +448,25 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int TYPE>
+template <int TYPE, bool GATED>
 cudaError_t launch_typed(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
-                         unsigned int* err, cudaStream_t s) {
+                         int64_t n_out, unsigned int* err, cudaStream_t s) {
     const size_t smem = 1024 + STAGES * (A_BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-    qgemm_kernel<TYPE><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, err);
+    qgemm_kernel<TYPE, GATED><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
-                         uint16_t* y, unsigned int* err, cudaStream_t s) {
+                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     CUtensorMap map;
@@ -457,9 +478,15 @@ cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int6
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
-    if (type == kQ4_K) return launch_typed<kQ4_K>(map, tiles, M, N, K, y, err, s);
-    if (type == kQ6_K) return launch_typed<kQ6_K>(map, tiles, M, N, K, y, err, s);
-    return launch_typed<kQ8_0>(map, tiles, M, N, K, y, err, s);
+    if (gated_n_out > 0) {
+        // interleaved gate/up: N = padded rows of both; BN = 128 keeps whole pairs per CTA
+        if (type == kQ4_K) return launch_typed<kQ4_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
+        if (type == kQ6_K) return launch_typed<kQ6_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
+        return launch_typed<kQ8_0, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
+    }
+    if (type == kQ4_K) return launch_typed<kQ4_K, false>(map, tiles, M, N, K, y, N, err, s);
+    if (type == kQ6_K) return launch_typed<kQ6_K, false>(map, tiles, M, N, K, y, N, err, s);
+    return launch_typed<kQ8_0, false>(map, tiles, M, N, K, y, N, err, s);
 }
 
 }  // namespace ocl

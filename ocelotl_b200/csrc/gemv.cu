@@ -625,7 +625,61 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
     }
 }
 
-template <int TYPE, int NT, bool TPF>
+constexpr int kEpiPlain = 0, kEpiTp = 1, kEpiGated = 2;
+
+// silu(z) * u with silu(z) = z * sigmoid(z) = z * (1 / (1 + exp(-z)))
+// (crates/kernels/src/mlp.rs:77-86, then the gate_buf *= up_buf loop at :227-230).
+__device__ __forceinline__ float silu_mul(float z, float u) { return z * (1.0f / (1.0f + expf(-z))) * u; }
+
+// Gated epilogue: the CTA's RT row tiles are RT/2 (gate, up) pairs.  With one
+// K split the CTA writes act = silu(gate) * up; with ks splits it writes gate
+// and up partials ([ks][rows][2][npad], npad = 16 * pairs) and the last CTA of
+// the group adds them in split order before applying silu * up.
+__device__ __forceinline__ void gated_epilogue(const GemvArgs& a, const float* red, int RT, int KW, int split) {
+    const int P = RT >> 1;
+    const int64_t o0 = (int64_t)blockIdx.x * P * 16, npad = (a.n_rt >> 1) * 16;
+    for (int idx = threadIdx.x; idx < P * 16 * a.rows; idx += blockDim.x) {
+        const int m = idx / (P * 16), pl = idx - m * P * 16;
+        const int pr = pl >> 4, row = pl & 15;
+        const int64_t o = o0 + pl;
+        if (o >= a.n) continue;
+        float gv = 0.f, uv = 0.f;
+        for (int q = 0; q < KW; ++q) {
+            gv += red[((q * RT + 2 * pr) * a.rows + m) * 16 + row];
+            uv += red[((q * RT + 2 * pr + 1) * a.rows + m) * 16 + row];
+        }
+        if (a.ks == 1) {
+            a.y[(int64_t)m * a.n + o] = silu_mul(gv, uv);
+        } else {
+            float* base = a.part + (((int64_t)split * a.rows + m) * 2) * npad;
+            base[o] = gv;
+            base[npad + o] = uv;
+        }
+    }
+    if (a.ks == 1) return;
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned int last_g;
+    if (threadIdx.x == 0) last_g = (atomicAdd(a.counters + blockIdx.x, 1u) == (unsigned)(a.ks - 1));
+    __syncthreads();
+    if (!last_g) return;
+    __threadfence();
+    const int64_t nr = min((int64_t)P * 16, a.n - o0);
+    for (int64_t idx = threadIdx.x; idx < nr * a.rows; idx += blockDim.x) {
+        const int m = (int)(idx / nr);
+        const int64_t o = o0 + (idx - (int64_t)m * nr);
+        float gv = 0.f, uv = 0.f;
+        for (int s2 = 0; s2 < a.ks; ++s2) {
+            const float* base = a.part + (((int64_t)s2 * a.rows + m) * 2) * npad;
+            gv += __ldcg(base + o);
+            uv += __ldcg(base + npad + o);
+        }
+        a.y[(int64_t)m * a.n + o] = silu_mul(gv, uv);
+    }
+    if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
+}
+
+template <int TYPE, int NT, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
     constexpr int UB = unit_bytes(TYPE), S = kStages, NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
@@ -788,46 +842,50 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 
     // 5. add the KW slices of each row tile in slice order; write y or a partial
     const int64_t r0 = (int64_t)blockIdx.x * RT * 16;
-    if constexpr (TPF) {  // row-split layer: sum over ranks through peer memory
+    if constexpr (EPI == kEpiTp) {  // row-split layer: sum over ranks through peer memory
         tp_epilogue(a, red, RT, KW, r0);
         return;
-    }
-    for (int idx = threadIdx.x; idx < RT * 16 * a.rows; idx += blockDim.x) {
-        const int m = idx / (RT * 16), rl = idx - m * RT * 16;
-        const int tile = rl >> 4, row = rl & 15;
-        const int64_t o = r0 + rl;
-        if (o >= a.n) continue;
-        float v = 0.f;
-        for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
-        if (a.ks == 1) a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
-        else a.part[((int64_t)split * a.rows + m) * a.n + o] = v;
-    }
-    if (a.ks == 1) return;
+    } else if constexpr (EPI == kEpiGated) {
+        gated_epilogue(a, red, RT, KW, split);
+        return;
+    } else {
+        for (int idx = threadIdx.x; idx < RT * 16 * a.rows; idx += blockDim.x) {
+            const int m = idx / (RT * 16), rl = idx - m * RT * 16;
+            const int tile = rl >> 4, row = rl & 15;
+            const int64_t o = r0 + rl;
+            if (o >= a.n) continue;
+            float v = 0.f;
+            for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
+            if (a.ks == 1) a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+            else a.part[((int64_t)split * a.rows + m) * a.n + o] = v;
+        }
+        if (a.ks == 1) return;
 
-    // 6. cross-CTA split: the last CTA of this row group adds in split order
-    __threadfence();
-    __syncthreads();
-    __shared__ unsigned int last;
-    if (threadIdx.x == 0) last = (atomicAdd(a.counters + blockIdx.x, 1u) == (unsigned)(a.ks - 1));
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    const int64_t nr = min((int64_t)RT * 16, a.n - r0);
-    for (int64_t idx = threadIdx.x; idx < nr * a.rows; idx += blockDim.x) {
-        const int m = (int)(idx / nr);
-        const int64_t o = r0 + (idx - (int64_t)m * nr);
-        float v = 0.f;
-        for (int s2 = 0; s2 < a.ks; ++s2) v += __ldcg(a.part + ((int64_t)s2 * a.rows + m) * a.n + o);
-        a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+        // 6. cross-CTA split: the last CTA of this row group adds in split order
+        __threadfence();
+        __syncthreads();
+        __shared__ unsigned int last;
+        if (threadIdx.x == 0) last = (atomicAdd(a.counters + blockIdx.x, 1u) == (unsigned)(a.ks - 1));
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        const int64_t nr = min((int64_t)RT * 16, a.n - r0);
+        for (int64_t idx = threadIdx.x; idx < nr * a.rows; idx += blockDim.x) {
+            const int m = (int)(idx / nr);
+            const int64_t o = r0 + (idx - (int64_t)m * nr);
+            float v = 0.f;
+            for (int s2 = 0; s2 < a.ks; ++s2) v += __ldcg(a.part + ((int64_t)s2 * a.rows + m) * a.n + o);
+            a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
+        }
+        if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
     }
-    if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
 }
 
-template <int TYPE, int NT, bool TPF>
+template <int TYPE, int NT, int EPI>
 cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
     static size_t configured = 0;  // per template instance: largest dynamic smem enabled so far
     if (pl.smem > 48 * 1024 && pl.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, TPF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)pl.smem);
         if (e != cudaSuccess) return e;
         configured = pl.smem;
@@ -842,26 +900,27 @@ cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT, TPF>, a);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT, EPI>, a);
 }
 
-template <int TYPE, bool TPF>
+template <int TYPE, int EPI>
 cudaError_t launch_nt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
     switch (pl.nt) {
-        case 0: return launch_typed<TYPE, 0, TPF>(pl, a, pdl, s);
-        case 1: return launch_typed<TYPE, 1, TPF>(pl, a, pdl, s);
-        case 2: return launch_typed<TYPE, 2, TPF>(pl, a, pdl, s);
-        case 3: return launch_typed<TYPE, 3, TPF>(pl, a, pdl, s);
-        case 4: return launch_typed<TYPE, 4, TPF>(pl, a, pdl, s);
-        case 5: return launch_typed<TYPE, 5, TPF>(pl, a, pdl, s);
-        case 6: return launch_typed<TYPE, 6, TPF>(pl, a, pdl, s);
+        case 0: return launch_typed<TYPE, 0, EPI>(pl, a, pdl, s);
+        case 1: return launch_typed<TYPE, 1, EPI>(pl, a, pdl, s);
+        case 2: return launch_typed<TYPE, 2, EPI>(pl, a, pdl, s);
+        case 3: return launch_typed<TYPE, 3, EPI>(pl, a, pdl, s);
+        case 4: return launch_typed<TYPE, 4, EPI>(pl, a, pdl, s);
+        case 5: return launch_typed<TYPE, 5, EPI>(pl, a, pdl, s);
+        case 6: return launch_typed<TYPE, 6, EPI>(pl, a, pdl, s);
         default: return cudaErrorInvalidValue;
     }
 }
 
 template <int TYPE>
 cudaError_t launch_tp(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
-    return a.tp.world > 1 ? launch_nt<TYPE, true>(pl, a, pdl, s) : launch_nt<TYPE, false>(pl, a, pdl, s);
+    if (a.gated) return launch_nt<TYPE, kEpiGated>(pl, a, pdl, s);
+    return a.tp.world > 1 ? launch_nt<TYPE, kEpiTp>(pl, a, pdl, s) : launch_nt<TYPE, kEpiPlain>(pl, a, pdl, s);
 }
 
 }  // namespace
@@ -922,6 +981,16 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
     pl.umax = (pl.n_units + ks - 1) / ks;
     pl.smem = (size_t)smem_map(type, pl.nt, pl.umax, rows).total;
     pl.part_floats = pl.ks > 1 ? (size_t)pl.ks * rows * n : 0;
+    return pl;
+}
+
+GemvPlan plan_gemv_gated(int type, int64_t n_gate, int64_t k, int rows, int sms) {
+    const int64_t n_pairs = (n_gate + 15) / 16;
+    GemvPlan pl = plan_gemv(type, 2 * n_pairs * 16, k, rows, sms);
+    if (pl.kw > kWarps / 2) {  // at least one whole (gate, up) pair of row tiles per CTA
+        pl.kw = kWarps / 2;
+        pl.groups = (pl.n_rt + (kWarps / pl.kw) - 1) / (kWarps / pl.kw);
+    }
     return pl;
 }
 
@@ -990,6 +1059,32 @@ cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const
     a.part = part;
     a.counters = counters;
     a.err = err;
+    if (type == kQ4_K) return launch_tp<kQ4_K>(pl, a, pdl, s);
+    if (type == kQ6_K) return launch_tp<kQ6_K>(pl, a, pdl, s);
+    return launch_tp<kQ8_0>(pl, a, pdl, s);
+}
+
+cudaError_t launch_gemv_gated(int type, const void* tiles, int64_t n_gate, int64_t k, const XPlanes& p, int rows,
+                              float* act, const GemvPlan& pl, float* part, unsigned int* counters, unsigned int* err,
+                              bool pdl, cudaStream_t s) {
+    if ((kWarps / pl.kw) % 2 != 0 || pl.n_rt % 2 != 0) return cudaErrorInvalidValue;
+    GemvArgs a{};
+    a.W = (const uint8_t*)tiles;
+    a.n = n_gate;
+    a.k = k;
+    a.n_rt = pl.n_rt;
+    a.n_units = pl.n_units;
+    a.nblk = (int)(k / 32);
+    a.ks = pl.ks;
+    a.rt_per_cta = kWarps / pl.kw;
+    a.umax = pl.umax;
+    a.p = p;
+    a.rows = rows;
+    a.y = act;
+    a.part = part;
+    a.counters = counters;
+    a.err = err;
+    a.gated = 1;
     if (type == kQ4_K) return launch_tp<kQ4_K>(pl, a, pdl, s);
     if (type == kQ6_K) return launch_tp<kQ6_K>(pl, a, pdl, s);
     return launch_tp<kQ8_0>(pl, a, pdl, s);

@@ -60,6 +60,9 @@ struct GemvPlan {
     size_t part_floats; // cross-CTA partial sums (0 when ks == 1)
 };
 GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms);
+// Plan for a gate/up pair stored as interleaved row tiles (tile 2t = gate tile
+// t, tile 2t+1 = up tile t; n_gate outputs): every CTA holds whole pairs.
+GemvPlan plan_gemv_gated(int type, int64_t n_gate, int64_t k, int rows, int sms);
 // Same plan without a cross-CTA K split (required by the fused all-reduce);
 // false if the CTA's activation planes then no longer fit in shared memory.
 bool plan_single_split(GemvPlan& pl, int type, int rows);
@@ -93,6 +96,7 @@ struct GemvArgs {
     unsigned int* counters;  // [groups], zero between launches
     unsigned int* err;       // [0] bad embedding ids, [1] bounded waits that gave up
     TpArgs tp;               // world > 1: sum the rows over ranks in the epilogue (ks must be 1)
+    int gated;               // 1: interleaved gate/up tiles, y = silu(gate) * up over n = n_gate outputs
 };
 
 // y [rows<=16, n] = planes . W^T (+ bias), geometry from plan_gemv.  `pdl`
@@ -101,9 +105,16 @@ struct GemvArgs {
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
                         unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp = nullptr);
+// act [rows<=16, n_gate] = silu(planes . Wg^T) * (planes . Wu^T) over an
+// interleaved gate/up weight, geometry from plan_gemv_gated.
+cudaError_t launch_gemv_gated(int type, const void* tiles, int64_t n_gate, int64_t k, const XPlanes& p, int rows,
+                              float* act, const GemvPlan& pl, float* part, unsigned int* counters, unsigned int* err,
+                              bool pdl, cudaStream_t s);
 
 // Prefill GEMM: y bf16 [M, N] = x bf16 [M, K] . W^T on tcgen05 (K a multiple of 256).
+// gated_n_out > 0: W is an interleaved gate/up pair with N = 2 * 16 * row tiles
+// of each, and y bf16 [M, gated_n_out] = silu(x . gate^T) * (x . up^T).
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
-                         uint16_t* y, unsigned int* err, cudaStream_t s);
+                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out = 0);
 
 }  // namespace ocl

@@ -92,3 +92,30 @@ def q_linear(ggml_type, blocks, x, rows, in_features, out_features, bias=None, t
     if fn(ggml_type, _p(b8), _p(x), rows, in_features, out_features, _p(b), _p(out), threads):
         raise RuntimeError("oracle q_linear failed")
     return out
+
+
+def silu_inplace(v: np.ndarray) -> np.ndarray:
+    """silu(z) = z * (1 / (1 + exp(-z))) in f32 (crates/kernels/src/mlp.rs:77-86)."""
+    v = np.asarray(v, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        sig = np.float32(1.0) / (np.float32(1.0) + np.exp(-v))
+    v *= sig
+    return v
+
+
+def q_gated(ggml_type, gate_blocks, up_blocks, x, rows, hidden, intermediate, threads=1) -> np.ndarray:
+    """silu(x . gate^T) * (x . up^T): mlp_gated_silu up to the down projection
+    (crates/kernels/src/mlp.rs:216-230), the matmuls as q_linear."""
+    g = q_linear(ggml_type, gate_blocks, x, rows, hidden, intermediate, threads=threads)
+    u = q_linear(ggml_type, up_blocks, x, rows, hidden, intermediate, threads=threads)
+    silu_inplace(g)
+    g *= u
+    return g
+
+
+def q_mlp_gated_silu(ggml_type, gate_blocks, up_blocks, down_type, down_blocks, x, rows, hidden, intermediate,
+                     threads=1) -> tuple[np.ndarray, np.ndarray]:
+    """(act, out) of mlp_gated_silu (crates/kernels/src/mlp.rs:139-240) on quantized weights."""
+    act = q_gated(ggml_type, gate_blocks, up_blocks, x, rows, hidden, intermediate, threads=threads)
+    out = q_linear(down_type, down_blocks, act, rows, intermediate, hidden, threads=threads)
+    return act, out

@@ -7,7 +7,7 @@ plain fp32 reference of the same op.  Tolerance 2e-2 (tests/tolerance.py).
 import pytest
 import torch
 
-from tests.tolerance import GEMM_FLOOR, GEMM_RTOL, normwise_err, rel_err
+from tests.tolerance import GEMM_FLOOR, GEMM_RTOL, gated_rel_err, normwise_err, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -44,3 +44,23 @@ def test_gemm_rejects_unaligned_k(backend):
     x = torch.zeros(64, 96, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(UnsupportedError):
         backend.gemm_bf16(x, w)
+
+
+@pytest.mark.parametrize("t", [12, 14, 8])
+@pytest.mark.parametrize("inter,k,rows", [(128, 256, 128), (200, 1024, 300), (14336, 4096, 512)])
+def test_gemm_gated(backend, t, inter, k, rows):
+    """Prefill gate+up over an interleaved pair with silu * up on the accumulators."""
+    from ocelotl_b200 import synth
+    g = backend.upload_quant(t, synth.quant_blocks(t, inter, k, 4, "gg", device="cuda"), inter, k)
+    u = backend.upload_quant(t, synth.quant_blocks(t, inter, k, 4, "gu", device="cuda"), inter, k)
+    pair = backend.pair_gated(g, u)
+    x = synth.activations(rows, k, 4, "gx", device="cuda", dtype=torch.bfloat16).contiguous()
+    act = backend.gemm_gated_bf16(pair, x)
+    torch.cuda.synchronize()
+    xf = x.float()
+    gy, uy = xf @ backend.dequant(g.quant).t(), xf @ backend.dequant(u.quant).t()
+    ref = (gy * torch.sigmoid(gy) * uy).cpu().numpy()
+    assert backend.take_device_errors() == (0, 0)
+    got = act.float().cpu().numpy()
+    e = gated_rel_err(got, gy.cpu().numpy(), uy.cpu().numpy())
+    assert e <= GEMM_RTOL, (e, normwise_err(got, ref))

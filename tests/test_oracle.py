@@ -144,3 +144,20 @@ def test_q_linear_avx2_threaded_bitwise(oracle):
 def test_oracle_rejects_bad_k(oracle):
     with pytest.raises(ValueError):
         oracle.dequant(12, np.zeros(144, np.uint8), 1, 100)
+
+
+def test_silu_hand_checked_values(oracle):
+    # silu(z) = z / (1 + e^-z): 0 -> 0, 1 -> 0.73105858, -1 -> -0.26894143, 2 -> 1.76159416, 3 -> 2.85772238
+    v = oracle.silu_inplace(np.array([0.0, 1.0, -1.0, 2.0, 3.0], np.float32))
+    assert np.allclose(v, [0.0, 0.73105858, -0.26894143, 1.76159416, 2.85772238], atol=1e-6)
+    # large negative: sigmoid underflows to 0, silu -> 0 (no NaN)
+    big = oracle.silu_inplace(np.array([-200.0, -1e30, 200.0], np.float32))
+    assert big[0] == 0 and big[1] == 0 and big[2] == 200.0
+
+
+def test_oracle_mlp_doc_example(oracle):
+    from tests.mlp_cases import doc_example
+    x, gate, up, down, hidden, inter = doc_example()
+    act, out = oracle.q_mlp_gated_silu(8, gate, up, 8, down, x, 1, hidden, inter)
+    assert np.allclose(act, 3.5231884, atol=1e-5)
+    assert np.allclose(out, 3.5231884, atol=1e-5)

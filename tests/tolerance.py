@@ -12,6 +12,12 @@ dequantized weights.  Here the weights themselves are rounded to bf16 (2^-9
 relative) before the tensor cores see them, so an output that cancels to ~0
 carries an absolute error of ~2^-9 * rms(r); a floor below rms would fail any
 correct bf16 kernel on such outputs.
+Gated bf16 GEMM (act = silu(g) * u): each factor carries the GEMM's absolute
+error ~eps * rms of its own column set, so the product's error is
+~eps * (|silu(g)| * rms(u) + |u| * rms(g)); that (or |act| if larger) is the
+denominator, the bound again GEMM_RTOL.  A floor at rms(act) alone fails a
+correct kernel wherever a large gate meets a small up (|g| ~ 3.5 rms, |u| ~ 0.2
+rms gives ~3e-2 for the exact f32 product of bf16-rounded weights).
 """
 import numpy as np
 
@@ -35,3 +41,16 @@ def normwise_err(y, r):
     r = np.asarray(r, dtype=np.float64)
     m = np.max(np.abs(r))
     return float(np.max(np.abs(y - r)) / (m if m else 1.0))
+
+
+def gated_rel_err(y, g, u):
+    """max |y - silu(g) u| / max(|silu(g) u|, |silu(g)| rms(u) + |u| rms(g))."""
+    y = np.asarray(y, dtype=np.float64)
+    g = np.asarray(g, dtype=np.float64)
+    u = np.asarray(u, dtype=np.float64)
+    with np.errstate(over="ignore"):
+        sg = g / (1.0 + np.exp(-g))
+    r = sg * u
+    den = np.maximum(np.abs(r), np.abs(sg) * np.sqrt(np.mean(u * u)) + np.abs(u) * np.sqrt(np.mean(g * g)))
+    den = np.where(den == 0, 1.0, den)
+    return float(np.max(np.abs(y - r) / den)) if r.size else 0.0
