@@ -46,10 +46,20 @@ namespace ocl {
 namespace {
 
 constexpr int kWarps = 8;   // warps per CTA
+// Ring depth per warp, by weight type and layout.  Measured on B200 (Llama-shaped
+// matrices, same-box A/B): for a single row, 4 stages beat 2 for Q4_K (2.3 KB
+// records) by 0.3-0.6 us per call; for Q6_K (3.3 KB records, 43 KB of planes
+// at K = 14336) more than 2 stages cost CTAs per SM and ran slower; Q8_0 units
+// are 4.3 KB; with two or more rows (bigger planes) 4 stages lost ~20%.
+#ifndef OCL_GEMV_STAGES_Q4
+#define OCL_GEMV_STAGES_Q4 4
+#endif
 #ifndef OCL_GEMV_STAGES
 #define OCL_GEMV_STAGES 2
 #endif
-constexpr int kStages = OCL_GEMV_STAGES;  // ring depth per warp
+__host__ __device__ constexpr int stages(int t, int nt) {
+    return (t == kQ4_K && nt == 0) ? OCL_GEMV_STAGES_Q4 : OCL_GEMV_STAGES;
+}
 
 __host__ __device__ constexpr int unit_bytes(int t) { return t == kQ4_K ? 2304 : t == kQ6_K ? 3360 : 4352; }
 __host__ __device__ constexpr int sum_per(int t) { return t == kQ4_K ? 8 : t == kQ6_K ? 16 : 0; }
@@ -518,8 +528,8 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
     const int sstride = sum_per(type) ? (nt ? umax * sum_per(type) : umax * sum_per(type) / 2) + 4 : 0;
     SmemMap m;
     m.ring = 0;
-    m.bars = kWarps * kStages * unit_bytes(type);
-    m.red = m.bars + (kWarps * kStages + 2) * 8;              // +1 barrier for the planes, padded
+    m.bars = kWarps * stages(type, nt) * unit_bytes(type);
+    m.red = m.bars + (kWarps * stages(type, nt) + 2) * 8;              // +1 barrier for the planes, padded
     m.xq = (m.red + kWarps * 16 * rows * 4 + 127) & ~127;      // per-warp folded outputs
     m.xsum = m.xq + ncp * qstride;
     m.xs = m.xsum + ncp * sstride * 4;
@@ -682,7 +692,7 @@ __device__ __forceinline__ void gated_epilogue(const GemvArgs& a, const float* r
 template <int TYPE, int NT, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
-    constexpr int UB = unit_bytes(TYPE), S = kStages, NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
+    constexpr int UB = unit_bytes(TYPE), S = stages(TYPE, NT), NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
     constexpr int NCP = NT ? 3 * MPAD : 3;  // plane rows copied from global
     constexpr int NTA = NT ? NT : 1;
     extern __shared__ __align__(128) uint8_t smem[];

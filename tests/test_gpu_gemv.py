@@ -122,3 +122,24 @@ def test_unsupported_before_launch(backend):
         backend.upload_quant(12, np.zeros(144, np.uint8), 1, 300)  # K % 256 != 0
     with pytest.raises(UnsupportedError):
         backend.linear_d(backend.alloc(4), 1, 4, backend.alloc(4), 1, None, backend.alloc(1))  # f32 weight
+
+
+@pytest.mark.parametrize("t,n,k", [(12, 1000, 2560), (14, 3000, 768), (8, 1000, 1184), (8, 4099, 4096),
+                                   (12, 37, 65536), (14, 150, 2048)])
+def test_gemv_single_row_balanced_ranges(backend, oracle, t, n, k):
+    """Single row: record ranges cut row tiles across warps and CTAs (ragged n, k, bias)."""
+    got, ref = run_case(backend, oracle, t, n, k, 1, seed=9)
+    e = rel_err(got, ref)
+    assert e <= GEMV_RTOL, (NAMES[t], n, k, e, normwise_err(got, ref))
+    assert backend.take_device_errors() == (0, 0)
+
+
+def test_gemv_single_row_is_deterministic(backend):
+    from ocelotl_b200 import synth
+    n, k = 14336, 4096
+    w = backend.upload_quant(12, synth.quant_blocks(12, n, k, 2, "w"), n, k)
+    x = backend.upload(synth.activations(1, k, 2, "x").numpy())
+    outs = [backend.alloc(n) for _ in range(3)]
+    for o in outs:
+        backend.linear_d(x, 1, k, w, n, None, o)
+    assert torch.equal(outs[0].device, outs[1].device) and torch.equal(outs[0].device, outs[2].device)
