@@ -645,6 +645,41 @@ def run_ocelotl(args):
     return 0
 
 
+def run_profile_case(args):
+    """Small single-GPU cases for ncu captures (a few launches, a few hundred MB at most).
+
+    gemv: 4 copies of one weight (> L2 together), 8 single-row calls.
+    gemm: one weight, 3 prefill GEMMs of `rows` bf16 activations.
+    --case-shape "type:n:k[:rows]" picks the matrix (default the gate projection).
+    """
+    import torch
+
+    from ocelotl_b200 import synth
+    from ocelotl_b200.backend import CudaKernelBackend
+    from ocelotl_b200.build import build
+    build()
+    be = CudaKernelBackend(0)
+    dev = torch.device("cuda", 0)
+    f = [int(v) for v in args.case_shape.split(":")]
+    t, n, k = f[:3]
+    if args.case == "gemv":
+        ws = [be.upload_quant(t, synth.quant_blocks(t, n, k, 1, f"w{c}", device=dev), n, k) for c in range(4)]
+        x = synth.activations(1, k, 1, "x", device=dev)
+        y = torch.empty(1, n, device=dev)
+        for i in range(8):
+            be.linear_dev(ws[i % 4], x, 1, y)
+    else:
+        rows = f[3] if len(f) > 3 else 2048
+        w = be.upload_quant(t, synth.quant_blocks(t, n, k, 1, "w", device=dev), n, k)
+        x = synth.activations(rows, k, 1, "x", device=dev, dtype=torch.bfloat16).contiguous()
+        for _ in range(3):
+            be.gemm_bf16(x, w)
+    torch.cuda.synchronize()
+    errs = be.take_device_errors()
+    print(json.dumps({"case": args.case, "shape": args.case_shape, "device_errors": list(errs)}))
+    return 0 if errs == (0, 0) else 1
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -662,8 +697,12 @@ def main():
     ap.add_argument("--fused-mlp", type=int, default=1,
                     help="also time the layer with gate+up as one fused gated pass (ocl_q_linear_gated)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--case", choices=["gemv", "gemm"], help="run a small profiling case instead of the bench")
+    ap.add_argument("--case-shape", default="12:14336:4096")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.case:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ocelotl(args)

@@ -20,6 +20,8 @@ struct ocl_ctx {
     std::mutex mu;
     std::string err;
     void* scratch = nullptr;  // x planes for the GEMV
+    char* io = nullptr;       // device staging of the host-slice calls (x, bias, y), grown on demand
+    size_t io_bytes = 0;
     size_t scratch_bytes = 0;
     float* part = nullptr;  // cross-CTA split-K partial sums
     size_t part_bytes = 0;
@@ -106,6 +108,22 @@ struct DeviceGuard {
         if (prev >= 0 && cur != prev) cudaSetDevice(prev);
     }
 };
+
+// Device staging for ocl_q_linear_host.  A per-call cudaMallocAsync /
+// cudaFreeAsync pair returned its memory to the driver at every stream
+// synchronisation (the default pool keeps nothing), which cost ~0.5 ms a call.
+int ensure_io(ocl_ctx* ctx, size_t bytes) {
+    if (ctx->io_bytes >= bytes) return OCL_OK;
+    if (ctx->io) {
+        OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        cudaFree(ctx->io);
+        ctx->io = nullptr;
+        ctx->io_bytes = 0;
+    }
+    OCL_CUDA(ctx, cudaMalloc((void**)&ctx->io, bytes), "cudaMalloc(io staging)");
+    ctx->io_bytes = bytes;
+    return OCL_OK;
+}
 
 int ensure_scratch(ocl_ctx* ctx, size_t bytes) {
     if (ctx->scratch_bytes >= bytes) return OCL_OK;
@@ -270,6 +288,7 @@ void ocl_cuda_destroy(ocl_ctx* ctx) {
         DeviceGuard guard(ctx->device);
         cudaStreamSynchronize(ctx->stream);
         if (ctx->scratch) cudaFree(ctx->scratch);
+        if (ctx->io) cudaFree(ctx->io);
         if (ctx->part) cudaFree(ctx->part);
         if (ctx->counters) cudaFree(ctx->counters);
         if (ctx->dev_flags) cudaFree(ctx->dev_flags);
@@ -418,8 +437,9 @@ int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size
     if (!x_host || !y_host) return fail(ctx, OCL_ERR_INVALID, "linear_out_by_in x/out pointer is null");
     DeviceGuard guard(ctx->device);
     const size_t xb = rows * in_features * 4, yb = rows * out_features * 4, bb = bias_host ? out_features * 4 : 0;
-    char* buf = nullptr;
-    OCL_CUDA(ctx, cudaMallocAsync((void**)&buf, xb + yb + bb + 512, ctx->stream), "cudaMallocAsync(io)");
+    rc = ensure_io(ctx, xb + yb + bb + 512);
+    if (rc) return rc;
+    char* buf = ctx->io;
     float* xd = (float*)buf;
     float* yd = (float*)(buf + ((xb + 255) & ~(size_t)255));
     float* bd = bias_host ? (float*)((char*)yd + ((yb + 255) & ~(size_t)255)) : nullptr;
@@ -429,7 +449,6 @@ int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size
         rc = q_linear_locked(ctx, w, xd, rows, bd, yd);
         if (rc == OCL_OK) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
     }
-    cudaFreeAsync(buf, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(ctx, e, "linear_out_by_in host path");
