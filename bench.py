@@ -272,6 +272,7 @@ def run_stack(be, args, torch, synth, dev):
         xs = {name: synth.activations(m, k, args.seed, f"stack.x.{name}", device=dev) for name, t, n, k, _ in LAYER}
         ys = {name: torch.empty(m, n, device=dev) for name, t, n, k, _ in LAYER}
         logits = torch.empty(m, vocab, device=dev)
+        next_ids = torch.empty(m, dtype=torch.int32, device=dev)
         xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
 
         def token():
@@ -280,6 +281,14 @@ def run_stack(be, args, torch, synth, dev):
                 for name, t, n, k, _ in LAYER:
                     be.linear_dev(ws[name], xs[xin[name]], m, ys[name])
             be.linear_dev(head, h, m, logits)
+            be.greedy_sample(logits, out=next_ids)
+
+        def head_only():
+            be.linear_dev(head, h, m, logits)
+            be.greedy_sample(logits, out=next_ids)
+        gh = graph_of(head_only, be, torch)
+        head_us = time_graphs([gh], 20, torch)
+        del gh
         g = graph_of(token, be, torch)
         for _ in range(3):
             g.replay()
@@ -294,10 +303,13 @@ def run_stack(be, args, torch, synth, dev):
         us = 1e3 * a.elapsed_time(b) / reps
         alg = wbytes_total + m * wbytes(8, 1, HIDDEN)
         res[str(m)] = {"token_us": round(us, 1), "tok_s": round(m / (us * 1e-6), 1),
-                       "GB/s": round(alg / (us * 1e-6) / 1e9, 1), "alg_bytes": alg}
+                       "GB/s": round(alg / (us * 1e-6) / 1e9, 1), "alg_bytes": alg,
+                       "head_argmax_us": round(head_us, 2),
+                       "head_GB/s": round(wbytes(Q6_K, vocab, HIDDEN) / (head_us * 1e-6) / 1e9, 1)}
         del g
     res["note"] = ("per decode step: Q8_0 embedding gather, 32 x (qkv, o, gate, up, down) quantized GEMVs and the "
-                   "Q6_K output head, one CUDA graph; linear layers only (no attention or norms)")
+                   "Q6_K output head + greedy argmax over the 128256 logits, one CUDA graph; linear layers only (no attention "
+                   "or norms); head_argmax_us = head GEMV + argmax alone")
     del layers, head, emb
     torch.cuda.synchronize()
     return res

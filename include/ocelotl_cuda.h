@@ -221,6 +221,14 @@ OCL_API int ocl_q_mlp_gated_silu(ocl_ctx* ctx, const ocl_qbuf* gate_up, const oc
 OCL_API int ocl_q_gemm_gated_bf16(ocl_ctx* ctx, const ocl_qbuf* gate_up, const uint16_t* x_dev, size_t rows,
                                   size_t hidden, size_t intermediate, uint16_t* act_dev);
 
+/* Greedy sampling (crates/runtime/src/sampling.rs:29 greedy_sample) on the
+ * device: ids_dev[r] = argmax of logits_dev row r ([rows, vocab] f32), the
+ * lowest index among equal maxima, -0.0 equal to +0.0, NaN never chosen --
+ * except that a NaN at index 0 makes the answer 0, as the reference's scan
+ * does.  vocab == 0 is OCL_ERR_INVALID ("greedy_sample requires at least one
+ * logit"); rows <= 65535.  Bit-exact with the reference. */
+OCL_API int ocl_argmax_f32(ocl_ctx* ctx, const float* logits_dev, size_t rows, size_t vocab, int32_t* ids_dev);
+
 /* Q8_0 embedding gather: out f32 [n_ids, k] = dequantized rows ids[i] of `table`
  * (ids int32 in device memory), bit-exact with the GGUF block arithmetic.  The
  * ids are only known on the device, so an id outside [0, n_rows) cannot fail the

@@ -50,6 +50,7 @@ SIGNATURES = {
     "ocl_q_linear_gated": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "ocl_q_mlp_gated_silu": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_gemm_gated_bf16": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "ocl_argmax_f32": (C.c_int, [_vp, _vp, _sz, _sz, _vp]),
     "ocl_q_embed_rows": (C.c_int, [_vp, _vp, _vp, _sz, _vp]),
     "ocl_take_device_errors": (C.c_int, [_vp, C.POINTER(C.c_uint), C.POINTER(C.c_uint)]),
 }

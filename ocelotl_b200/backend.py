@@ -415,3 +415,26 @@ class CudaKernelBackend:
             if temp is not None:
                 self.synchronize()
                 temp.quant.free()
+
+    # -- greedy sampling (crates/runtime/src/sampling.rs:29) ----------------------
+    def greedy_sample(self, logits, out: torch.Tensor | None = None):
+        """Argmax per row of f32 logits with greedy_sample's tie and NaN rules.
+
+        logits: a contiguous f32 tensor on this device ([vocab] or [rows, vocab]),
+        returning int32 ids on the device; or a host f32 array of one row,
+        returning the id as an int (copied in and out).
+        """
+        if not isinstance(logits, torch.Tensor):
+            arr = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1)
+            if arr.size == 0:
+                raise _kernel_err("greedy_sample requires at least one logit")
+            ids = self.greedy_sample(torch.from_numpy(arr).to(self.torch_device))
+            return int(ids.cpu()[0])
+        if logits.dtype != torch.float32 or not logits.is_contiguous() or logits.device != self.torch_device:
+            raise _kernel_err("greedy_sample logits must be a contiguous f32 tensor on " + str(self.torch_device))
+        rows, vocab = (1, logits.numel()) if logits.dim() == 1 else (logits.shape[0], logits.shape[-1])
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int32, device=self.torch_device)
+        self._check(self._lib.ocl_argmax_f32(self._ctx, C.c_void_p(logits.data_ptr()), rows, vocab,
+                                             C.c_void_p(out.data_ptr())))
+        return out

@@ -20,6 +20,8 @@ struct ocl_ctx {
     std::mutex mu;
     std::string err;
     void* scratch = nullptr;  // x planes for the GEMV
+    unsigned long long* amax_slots = nullptr;  // argmax: per-row best key, zero between launches
+    unsigned int* amax_counters = nullptr;     // argmax: per-row CTA arrivals, zero between launches
     char* io = nullptr;       // device staging of the host-slice calls (x, bias, y), grown on demand
     size_t io_bytes = 0;
     size_t scratch_bytes = 0;
@@ -289,6 +291,8 @@ void ocl_cuda_destroy(ocl_ctx* ctx) {
         cudaStreamSynchronize(ctx->stream);
         if (ctx->scratch) cudaFree(ctx->scratch);
         if (ctx->io) cudaFree(ctx->io);
+        if (ctx->amax_slots) cudaFree(ctx->amax_slots);
+        if (ctx->amax_counters) cudaFree(ctx->amax_counters);
         if (ctx->part) cudaFree(ctx->part);
         if (ctx->counters) cudaFree(ctx->counters);
         if (ctx->dev_flags) cudaFree(ctx->dev_flags);
@@ -717,6 +721,34 @@ int ocl_q_gemm_gated_bf16(ocl_ctx* ctx, const ocl_qbuf* gate_up, const uint16_t*
              ocl::launch_qgemm(gate_up->type, gate_up->dev, (int64_t)rows, n_int, (int64_t)hidden, x_dev, act_dev,
                                ctx->dev_flags, ctx->stream, (int64_t)intermediate),
              "q_gemm_gated launch");
+    return OCL_OK;
+}
+
+int ocl_argmax_f32(ocl_ctx* ctx, const float* logits_dev, size_t rows, size_t vocab, int32_t* ids_dev) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (vocab == 0) return fail(ctx, OCL_ERR_INVALID, "greedy_sample requires at least one logit");
+    if (rows == 0) return OCL_OK;
+    if (!logits_dev || !ids_dev) return fail(ctx, OCL_ERR_INVALID, "argmax: null argument");
+    if (rows > (size_t)ocl::kArgmaxRowsMax || vocab > 0x7FFFFFFFu)
+        return fail(ctx, OCL_ERR_UNSUPPORTED,
+                    "unsupported feature `argmax shape` (requested `%zu x %zu`): supported = [rows <= %d, vocab < 2^31]",
+                    rows, vocab, ocl::kArgmaxRowsMax);
+    DeviceGuard guard(ctx->device);
+    if (!ctx->amax_slots) {
+        OCL_CUDA(ctx, cudaMalloc((void**)&ctx->amax_slots, ocl::kArgmaxRowsMax * sizeof(unsigned long long)),
+                 "cudaMalloc(argmax slots)");
+        OCL_CUDA(ctx, cudaMalloc((void**)&ctx->amax_counters, ocl::kArgmaxRowsMax * sizeof(unsigned int)),
+                 "cudaMalloc(argmax counters)");
+        OCL_CUDA(ctx, cudaMemsetAsync(ctx->amax_slots, 0, ocl::kArgmaxRowsMax * sizeof(unsigned long long), ctx->stream),
+                 "memset argmax slots");
+        OCL_CUDA(ctx, cudaMemsetAsync(ctx->amax_counters, 0, ocl::kArgmaxRowsMax * sizeof(unsigned int), ctx->stream),
+                 "memset argmax counters");
+    }
+    OCL_CUDA(ctx,
+             ocl::launch_argmax(logits_dev, (int64_t)rows, (int64_t)vocab, ids_dev, ctx->amax_slots,
+                                ctx->amax_counters, ctx->stream),
+             "argmax launch");
     return OCL_OK;
 }
 

@@ -111,6 +111,12 @@ cudaError_t launch_gemv_gated(int type, const void* tiles, int64_t n_gate, int64
                               float* act, const GemvPlan& pl, float* part, unsigned int* counters, unsigned int* err,
                               bool pdl, cudaStream_t s);
 
+// Greedy argmax per row of f32 logits (greedy_sample semantics); slots and
+// counters [rows] must be zero and are left zero.
+constexpr int kArgmaxRowsMax = 65535;
+cudaError_t launch_argmax(const float* logits, int64_t rows, int64_t vocab, int32_t* ids,
+                          unsigned long long* slots, unsigned int* counters, cudaStream_t s);
+
 // Prefill GEMM: y bf16 [M, N] = x bf16 [M, K] . W^T on tcgen05 (K a multiple of 256).
 // gated_n_out > 0: W is an interleaved gate/up pair with N = 2 * 16 * row tiles
 // of each, and y bf16 [M, gated_n_out] = silu(x . gate^T) * (x . up^T).

@@ -119,3 +119,29 @@ def q_mlp_gated_silu(ggml_type, gate_blocks, up_blocks, down_type, down_blocks, 
     act = q_gated(ggml_type, gate_blocks, up_blocks, x, rows, hidden, intermediate, threads=threads)
     out = q_linear(down_type, down_blocks, act, rows, intermediate, hidden, threads=threads)
     return act, out
+
+
+def greedy_sample(logits) -> int:
+    """greedy_sample (crates/runtime/src/sampling.rs:29-52): scan from index 0,
+    move only on a strictly greater value.  Raises ValueError on no logits."""
+    v = np.asarray(logits, dtype=np.float32).reshape(-1)
+    if v.size == 0:
+        raise ValueError("greedy_sample requires at least one logit")
+    best_idx, best_val = 0, v[0]
+    for i in range(1, v.size):
+        if v[i] > best_val:
+            best_idx, best_val = i, v[i]
+    return best_idx
+
+
+def greedy_sample_fast(logits) -> int:
+    """Vectorised form of greedy_sample for large vocabularies (same answer):
+    a NaN at index 0 is never displaced; otherwise NaNs never win and the first
+    maximum is taken (-0.0 == +0.0 under numpy's comparison too)."""
+    v = np.asarray(logits, dtype=np.float32).reshape(-1)
+    if v.size == 0:
+        raise ValueError("greedy_sample requires at least one logit")
+    if np.isnan(v[0]):
+        return 0
+    w = np.where(np.isnan(v), -np.inf, v)
+    return int(np.argmax(w))

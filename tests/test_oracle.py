@@ -161,3 +161,30 @@ def test_oracle_mlp_doc_example(oracle):
     act, out = oracle.q_mlp_gated_silu(8, gate, up, 8, down, x, 1, hidden, inter)
     assert np.allclose(act, 3.5231884, atol=1e-5)
     assert np.allclose(out, 3.5231884, atol=1e-5)
+
+
+def test_greedy_sample_reference_cases(oracle):
+    # peak at 3; three-way tie at 1, 2, 3 -> lowest id
+    assert oracle.greedy_sample([0.1, 0.5, 0.3, 0.9, 0.2]) == 3
+    assert oracle.greedy_sample([0.1, 0.5, 0.5, 0.5, 0.2]) == 1
+    assert oracle.greedy_sample([7.0]) == 0
+    with pytest.raises(ValueError):
+        oracle.greedy_sample([])
+    nan = float("nan")
+    assert oracle.greedy_sample([nan, 5.0, 9.0]) == 0        # NaN at 0 is never displaced
+    assert oracle.greedy_sample([1.0, nan, 0.5, nan]) == 0   # NaN never wins
+    assert oracle.greedy_sample([-0.0, 0.0]) == 0            # -0.0 == +0.0
+    assert oracle.greedy_sample([-np.inf, -np.inf]) == 0
+    assert oracle.greedy_sample([1.0, np.inf, np.inf]) == 1
+
+
+def test_greedy_sample_fast_matches_scan(oracle):
+    rng = np.random.default_rng(5)
+    for trial in range(300):
+        n = int(rng.integers(1, 40))
+        v = rng.integers(-3, 4, size=n).astype(np.float32)   # many ties
+        mask = rng.random(n) < 0.15
+        v[mask] = np.nan
+        if rng.random() < 0.2:
+            v[rng.integers(0, n)] = -0.0
+        assert oracle.greedy_sample_fast(v) == oracle.greedy_sample(v), v
