@@ -10,10 +10,13 @@ graph; weights rotate over enough distinct copies (>= 4x the 126 MB L2) that
 every step streams its weights from HBM.
 
 metric: algorithmic bytes (quantized weights + f32 activations in + outputs out)
-of the layer / time, GB/s.  With --gpus N (torchrun) the layer runs tensor
-parallel: q/k/v, gate, up split by output rows, o and down split by input
-columns with an NCCL all-reduce of their outputs; total work is fixed
-(strong scaling).
+of the layer / time, GB/s.  With --gpus N (torchrun), by default every GPU
+runs the whole layer on its own decode batch (replicas: the 8B layer needs no
+exchange step; value = all GPUs' bytes / max-over-ranks time, weak scaling).
+--mode tp splits the layer instead: q/k/v, gate, up by output rows, o and down
+by input columns with their outputs summed over ranks inside the GEMV (NVLink
+peer memory; NCCL with --nccl); total work fixed (strong scaling).  The
+70B-shaped layer is always timed tensor parallel over the N GPUs.
 
 --impl reference times the reference's CPU algorithm (the C restatement in
 oracle/: GGUF dequant + sequential-k f32 linear_out_by_in) on the host cores.
@@ -324,7 +327,7 @@ LAYER_70B = [  # hidden 8192, GQA kv 1024 (q 8192 + k 1024 + v 1024), ffn 28672
 ]
 
 
-def run_tp70b(be, args, torch, synth, dev, rank, tp, comm):
+def run_tp70b(be, args, torch, synth, dev, rank, tp, comm, group):
     """one Llama-3-70B-shaped layer's projections under tensor parallelism (per decode token)."""
     from ocelotl_b200.tp import TPLinear
     import torch.distributed as dist
@@ -334,7 +337,7 @@ def run_tp70b(be, args, torch, synth, dev, rank, tp, comm):
     layers = []
     for c in range(copies):
         layers.append({nm: TPLinear(be, t, synth.quant_blocks(t, n, k, args.seed, f"70b.{nm}.r{rank}.c{c}", device=dev),
-                                    n, k, "out" if sp == "col" else "in", comm=comm)
+                                    n, k, "out" if sp == "col" else "in", comm=comm, group=group)
                        for nm, t, n, k, sp in shards})
     total = sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER_70B)
     out = {"per_gpu_weight_bytes": per_gpu, "layer_weight_bytes": total, "copies": copies}
@@ -366,7 +369,7 @@ def run_tp70b(be, args, torch, synth, dev, rank, tp, comm):
         torch.cuda.synchronize()
         us = 1e3 * a.elapsed_time(b) / reps
         if tp > 1:
-            t_ = torch.tensor([us], device=dev)
+            t_ = torch.tensor([us])
             dist.all_reduce(t_, op=dist.ReduceOp.MAX)
             us = float(t_.item())
         out[str(m)] = {"layer_us": round(us, 1), "GB/s": round(total / (us * 1e-6) / 1e9, 1),
@@ -439,27 +442,43 @@ def run_ocelotl(args):
     dev = torch.device("cuda", torch.cuda.current_device())
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+        # The default group is gloo (host-side barriers and the max-over-ranks
+        # timing); an NCCL group is created only for the tensor-parallel steps.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
     if rank == 0:
         build()
     if world > 1:
         dist.barrier()
     be = CudaKernelBackend(dev.index)
-    m, tp = args.rows, world
+    m = args.rows
+    # replicas: every GPU runs the whole layer on its own decode batch (the 8B
+    # layer fits one GPU many times over; no exchange step), weak scaling.
+    # tp: the layer split over the GPUs (o/down sum over ranks), strong scaling.
+    tp = world if args.mode == "tp" else 1
+    replicas = world // tp
 
     shards = [(name, t, n // tp, k, sp) if sp == "col" else (name, t, n, k // tp, sp) for name, t, n, k, sp in LAYER]
     sh = {name: (t, n, k, sp) for name, t, n, k, sp in shards}
     rank_wbytes = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
     copies = max(2, -(-4 * L2_BYTES // rank_wbytes))
     # row-split layers sum over ranks inside the GEMV (peer memory); NCCL with --nccl
-    comm = TPComm(be, rank, tp, max_elems=16 * 8192) if (tp > 1 and not args.nccl) else None
+    comm = TPComm(be, rank, world, max_elems=16 * 8192) if (world > 1 and not args.nccl) else None
+    layer_comm = comm if tp > 1 else None
+    nccl_group = [dist.new_group(backend="nccl")] if tp > 1 else [None]
+
+    def nccl():
+        if nccl_group[0] is None:
+            nccl_group[0] = dist.new_group(backend="nccl")
+        return nccl_group[0]
     weights = []
     for c in range(copies):
         ws = {}
         for name, t, n, k, sp in shards:
             # this rank's shard, generated in place (same distribution as a sharded full weight)
             blocks = synth.quant_blocks(t, n, k, args.seed, f"{name}.r{rank}.c{c}", device=dev)
-            ws[name] = TPLinear(be, t, blocks, n, k, "out" if sp == "col" else "in", comm=comm)
+            # a replica's layer is whole: no split, no cross-rank sum
+            ws[name] = TPLinear(be, t, blocks, n, k, "out" if (sp == "col" or tp == 1) else "in", comm=layer_comm,
+                                group=nccl_group[0])
             del blocks
         weights.append(ws)
     torch.cuda.synchronize()
@@ -500,11 +519,11 @@ def run_ocelotl(args):
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     if world > 1:
-        t_ = torch.tensor([ms], device=dev)
+        t_ = torch.tensor([ms])
         dist.all_reduce(t_, op=dist.ReduceOp.MAX)
         ms = float(t_.item())
     ms_step = ms / args.steps
-    gbs = layer_alg_bytes(m) / (ms_step * 1e-3) / 1e9
+    gbs = replicas * layer_alg_bytes(m) / (ms_step * 1e-3) / 1e9
 
     # ---- per-projection call time (split + GEMV), graphs of back-to-back calls
     proj = {}
@@ -542,8 +561,8 @@ def run_ocelotl(args):
     # ---- end to end through the C ABI with host buffers ----------------------
     pinned_x = {name: xs[name].cpu().pin_memory() for name in xs}
     pinned_y = {name: torch.empty(m * sh[name][1], dtype=torch.float32).pin_memory() for name in ys}
-    h2d = sum(pinned_x[nm].numel() * 4 for nm in ("qkv", "o", "gate", "down"))
-    d2h = sum(pinned_y[nm].numel() * 4 for nm in pinned_y)
+    h2d = replicas * sum(pinned_x[nm].numel() * 4 for nm in ("qkv", "o", "gate", "down"))
+    d2h = replicas * sum(pinned_y[nm].numel() * 4 for nm in pinned_y)
 
     def e2e_step(i):
         ws = weights[i % copies]
@@ -552,7 +571,7 @@ def run_ocelotl(args):
                                 pinned_y[name].numpy())
             if sp == "row" and tp > 1:
                 y = pinned_y[name].to(dev)
-                dist.all_reduce(y)
+                dist.all_reduce(y, group=nccl_group[0])
                 pinned_y[name].copy_(y.cpu())
 
     for i in range(max(3, args.warmup)):
@@ -566,10 +585,10 @@ def run_ocelotl(args):
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     if world > 1:
-        t_ = torch.tensor([e2e_s], device=dev)
+        t_ = torch.tensor([e2e_s])
         dist.all_reduce(t_, op=dist.ReduceOp.MAX)
         e2e_s = float(t_.item())
-    e2e_gbs = layer_alg_bytes(m) * args.steps / e2e_s / 1e9
+    e2e_gbs = replicas * layer_alg_bytes(m) * args.steps / e2e_s / 1e9
 
     # ---- decode batch sweep (configs[1]: M = 1, 2, 4, 8, 16), graphs ----------
     sweep = {}
@@ -599,7 +618,8 @@ def run_ocelotl(args):
 
     fused = run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev) if (args.fused_mlp and tp == 1) \
         else None
-    tp70 = run_tp70b(be, args, torch, synth, dev, rank, tp, comm) if args.tp70b else None
+    tp70 = run_tp70b(be, args, torch, synth, dev, rank, world, comm, nccl() if world > 1 else None) \
+        if args.tp70b else None
     prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
     stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
     errs = be.take_device_errors()
@@ -611,12 +631,13 @@ def run_ocelotl(args):
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong" if args.mode == "tp" else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init GGUF blocks generated on device, N(0,1) activations)",
-            "config": {"workload": WORKLOAD, "rows": m, "parallelism": f"tp{world}",
+            "config": {"workload": WORKLOAD, "rows": m,
+                       "parallelism": f"tp{world}" if args.mode == "tp" else f"replicas{world}",
                        "l2": f"inputs larger than L2: weights rotate over {copies} distinct copies "
                              f"({copies * rank_wbytes / 1e6:.0f} MB per GPU, >= 4x the 126 MB L2)",
-                       "alg_bytes_per_step": layer_alg_bytes(m),
+                       "alg_bytes_per_step": replicas * layer_alg_bytes(m),
                        "pct_of_8TBps": round(100 * gbs / 8000.0, 2),
                        "step": "CUDA graph of 5 ocl_q_linear calls" + ("" if tp == 1 else (
                            " + 2 NCCL all-reduces (o, down)" if args.nccl else
@@ -702,6 +723,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0x0CE107)
     ap.add_argument("--sweep", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["replicas", "tp"], default="replicas",
+                    help="N > 1: independent full layers per GPU (weak scaling) or one layer split over the GPUs")
     ap.add_argument("--nccl", action="store_true", help="TP: NCCL all-reduce instead of the fused one")
     ap.add_argument("--tp70b", type=int, default=1, help="also time configs[4] (70B-shaped layer, TP = N)")
     ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
