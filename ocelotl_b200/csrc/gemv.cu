@@ -952,6 +952,14 @@ GemvPlan plan_gemv(int type, int64_t n, int64_t k, int rows, int sms) {
         while (kw < 4 && kw * 2 <= pl.n_units / 2 && target >= kw * 1.5) kw *= 2;
         // never leave SMs without a CTA
         while (kw < kWarps && kw * 2 <= pl.n_units / 2 && (pl.n_rt + kWarps / kw - 1) / (kWarps / kw) < sms) kw *= 2;
+        // ... but not at the price of a second wave: when the planes of a long
+        // K leave room for one CTA per SM (two rows, K = 14336), halve kw while
+        // that brings the grid within one wave (measured: down at M = 2,
+        // 19.6 -> 16.7 us)
+        const size_t per_cta = (size_t)smem_map(type, pl.nt, pl.n_units, rows).total + 1024;
+        const int64_t slots = (int64_t)sms * (int64_t)((228 * 1024) / per_cta);
+        auto groups_of = [&](int kw_) { return (pl.n_rt + kWarps / kw_ - 1) / (kWarps / kw_); };
+        while (kw > 1 && groups_of(kw) > slots && groups_of(kw / 2) <= slots) kw /= 2;
     }
     int ks = 1;
     if (rows > 2) {
