@@ -6,7 +6,7 @@
 // One CTA computes a 256 (tokens) x 128 (output features) tile as two 128 x 128
 // accumulators in tensor memory that share each dequantized weight tile:
 //   * warp 8 (one lane) streams x tiles [256 x 64] bf16 with TMA (tiled,
-//     128-byte swizzle, no multicast) into a 4-stage shared-memory ring;
+//     128-byte swizzle, no multicast) into a 4- or 2-stage shared-memory ring;
 //   * warps 0-7 dequantize the matching weight tile [128 features x 64 k] from
 //     the TILED16 records (prefetched one 256-k unit ahead in registers) into
 //     bf16, written directly in the 128-byte-swizzled K-major layout the UMMA
@@ -29,7 +29,12 @@ namespace ocl {
 
 namespace {
 
-constexpr int BM = 256, BN = 128, BK = 64, STAGES = 4;       // BM = two 128-row MMA tiles sharing B
+constexpr int BM = 256, BN = 128, BK = 64;  // BM = two 128-row MMA tiles sharing B
+// Two shapes of the same kernel: 4 pipeline stages and one CTA per SM, or 2
+// stages and two CTAs per SM (<= 96 registers a thread, 2 x 256 TMEM columns),
+// which overlaps one CTA's epilogue and pipeline fill with the other's main
+// loop.  Measured on B200: the two-CTA form is 3-22% faster once the tile
+// grid exceeds one wave of SMs and 7-21% slower below that.
 constexpr int MMA_M = 128, ACCS = BM / MMA_M;                  // accumulators in TMEM (BN columns each)
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;  // 32 KB + 16 KB per stage
 constexpr int PRODUCER_WARPS = 8, TMA_WARP = 8, MMA_WARP = 9, THREADS = 320;
@@ -259,8 +264,8 @@ __device__ __forceinline__ void dequant_quarter(const UnitRegs& R, int qt, int r
 // 2t+1 = up tile t; N = their total padded rows) and y [M, n_out] =
 // silu(gate) * up: each 32-column accumulator slice a thread reads is one
 // (gate, up) pair of 16-row tiles.
-template <int TYPE, bool GATED>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int TYPE, bool GATED, int STAGES>
+__global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, int64_t M, int64_t N,
                  int64_t K, uint16_t* __restrict__ y, int64_t n_out, unsigned int* __restrict__ err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -448,19 +453,30 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int TYPE, bool GATED>
-cudaError_t launch_typed(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
-                         int64_t n_out, unsigned int* err, cudaStream_t s) {
+template <int TYPE, bool GATED, int STAGES>
+cudaError_t launch_staged(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
+                          int64_t n_out, unsigned int* err, cudaStream_t s) {
     const size_t smem = 1024 + STAGES * (A_BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-    qgemm_kernel<TYPE, GATED><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err);
+    qgemm_kernel<TYPE, GATED, STAGES><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err);
     return cudaGetLastError();
+}
+
+template <int TYPE, bool GATED>
+cudaError_t launch_typed(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
+                         int64_t n_out, unsigned int* err, cudaStream_t s) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    if (tiles > sms) return launch_staged<TYPE, GATED, 2>(map, w, M, N, K, y, n_out, err, s);
+    return launch_staged<TYPE, GATED, 4>(map, w, M, N, K, y, n_out, err, s);
 }
 
 }  // namespace
