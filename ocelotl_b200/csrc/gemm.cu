@@ -457,8 +457,11 @@ template <int TYPE, bool GATED, int STAGES>
 cudaError_t launch_staged(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
                           int64_t n_out, unsigned int* err, cudaStream_t s) {
     const size_t smem = 1024 + STAGES * (A_BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
-    static bool configured = false;
-    if (!configured) {
+    static bool configured_by_dev[kMaxDevices] = {};  // a function attribute is set per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    bool& configured = configured_by_dev[dev < kMaxDevices ? dev : 0];
+    if (!configured || dev >= kMaxDevices) {
         cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;

@@ -893,8 +893,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 
 template <int TYPE, int NT, int EPI>
 cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
-    static size_t configured = 0;  // per template instance: largest dynamic smem enabled so far
-    if (pl.smem > 48 * 1024 && pl.smem > configured) {
+    // Largest dynamic shared memory enabled so far, per template instance and
+    // device (a function attribute is set per device).
+    static size_t configured_by_dev[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    size_t& configured = configured_by_dev[dev < kMaxDevices ? dev : 0];
+    if (pl.smem > 48 * 1024 && (pl.smem > configured || dev >= kMaxDevices)) {
         cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)pl.smem);
         if (e != cudaSuccess) return e;

@@ -23,6 +23,7 @@ struct XPlanes {
     int kx;        // K rounded up to a multiple of 256
 };
 
+constexpr int kMaxDevices = 64;  // per-device host-side caches
 constexpr int kRowsMax = 16;            // activation rows per GEMV launch
 constexpr int kColsMax = 3 * kRowsMax;  // int8 planes per launch
 
