@@ -131,8 +131,11 @@ OCL_API int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_bloc
 OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, size_t rows,
                  size_t in_features, size_t out_features, const float* bias_dev, float* y_dev);
 
-/* Same with host buffers (x, bias, y in host memory); copies in, runs, copies out
- * on the context stream and synchronises.  The slice-based linear_out_by_in. */
+/* Same with host buffers (x, bias, y in host memory), on the context stream,
+ * synchronising before it returns.  The slice-based linear_out_by_in.
+ * Page-locked (pinned) buffers are read and written by the kernels in place
+ * through unified addressing; pageable ones are copied through a device staging
+ * area kept by the context.  (Environment OCL_HOST_ZEROCOPY=0 forces staging.) */
 OCL_API int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size_t rows,
                       size_t in_features, size_t out_features, const float* bias_host,
                       float* y_host);

@@ -6,6 +6,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -125,6 +126,25 @@ int ensure_io(ocl_ctx* ctx, size_t bytes) {
     OCL_CUDA(ctx, cudaMalloc((void**)&ctx->io, bytes), "cudaMalloc(io staging)");
     ctx->io_bytes = bytes;
     return OCL_OK;
+}
+
+bool zero_copy_enabled() {
+    static const bool on = [] {
+        const char* f = getenv("OCL_HOST_ZEROCOPY");  // 0 forces the staged copies
+        return f ? atoi(f) != 0 : true;
+    }();
+    return on;
+}
+
+// Device address of a page-locked host buffer, or nullptr for pageable memory.
+const float* mapped(const float* host) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+        cudaGetLastError();  // clear
+        return nullptr;
+    }
+    if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+    return (const float*)at.devicePointer;
 }
 
 int ensure_scratch(ocl_ctx* ctx, size_t bytes) {
@@ -441,17 +461,31 @@ int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size
     if (!x_host || !y_host) return fail(ctx, OCL_ERR_INVALID, "linear_out_by_in x/out pointer is null");
     DeviceGuard guard(ctx->device);
     const size_t xb = rows * in_features * 4, yb = rows * out_features * 4, bb = bias_host ? out_features * 4 : 0;
+    // Page-locked host buffers are read and written by the kernels in place
+    // (mapped through unified addressing): no staging copies, no copy-engine
+    // round trips.  Pageable buffers go through the device staging area.
+    const float* xd = zero_copy_enabled() ? mapped(x_host) : nullptr;
+    float* yd = zero_copy_enabled() ? const_cast<float*>(mapped(y_host)) : nullptr;
+    const float* bd = (bias_host && zero_copy_enabled()) ? mapped(bias_host) : nullptr;
     rc = ensure_io(ctx, xb + yb + bb + 512);
     if (rc) return rc;
     char* buf = ctx->io;
-    float* xd = (float*)buf;
-    float* yd = (float*)(buf + ((xb + 255) & ~(size_t)255));
-    float* bd = bias_host ? (float*)((char*)yd + ((yb + 255) & ~(size_t)255)) : nullptr;
-    cudaError_t e = cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, ctx->stream);
-    if (e == cudaSuccess && bd) e = cudaMemcpyAsync(bd, bias_host, bb, cudaMemcpyHostToDevice, ctx->stream);
+    cudaError_t e = cudaSuccess;
+    if (!xd) {
+        e = cudaMemcpyAsync(buf, x_host, xb, cudaMemcpyHostToDevice, ctx->stream);
+        xd = (const float*)buf;
+    }
+    float* y_stage = (float*)(buf + ((xb + 255) & ~(size_t)255));
+    if (bias_host && !bd && e == cudaSuccess) {
+        float* b_stage = (float*)((char*)y_stage + ((yb + 255) & ~(size_t)255));
+        e = cudaMemcpyAsync(b_stage, bias_host, bb, cudaMemcpyHostToDevice, ctx->stream);
+        bd = b_stage;
+    }
+    const bool y_mapped = yd != nullptr;
+    if (!y_mapped) yd = y_stage;
     if (e == cudaSuccess) {
         rc = q_linear_locked(ctx, w, xd, rows, bd, yd);
-        if (rc == OCL_OK) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
+        if (rc == OCL_OK && !y_mapped) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (rc) return rc;

@@ -153,7 +153,8 @@ __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, 
     const int b = blockIdx.x, m = blockIdx.y, lane = threadIdx.x;
     const int64_t k0 = (int64_t)b * 256 + lane * 8;
     float v[8];
-    if (m < rows && (k & 3) == 0 && k0 + 8 <= k) {
+    // vector loads only where the row start is 16-byte aligned (any f32 pointer is accepted)
+    if (m < rows && (k & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && k0 + 8 <= k) {
         const float4 a = *reinterpret_cast<const float4*>(x + (int64_t)m * k + k0);
         const float4 c = *reinterpret_cast<const float4*>(x + (int64_t)m * k + k0 + 4);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;

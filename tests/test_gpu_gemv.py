@@ -143,3 +143,40 @@ def test_gemv_single_row_is_deterministic(backend):
     for o in outs:
         backend.linear_d(x, 1, k, w, n, None, o)
     assert torch.equal(outs[0].device, outs[1].device) and torch.equal(outs[0].device, outs[2].device)
+
+
+@pytest.mark.parametrize("pinned", [False, True])
+@pytest.mark.parametrize("rows", [1, 3, 20])
+def test_linear_out_by_in_pinned_and_pageable(backend, oracle, pinned, rows):
+    """Host-slice form: pinned buffers are used by the kernels in place, pageable ones are staged."""
+    from ocelotl_b200 import synth
+    n, k = 300, 1024
+    blocks = synth.quant_blocks(12, n, k, 8, "w")
+    w = backend.upload_quant(12, blocks, n, k)
+    x = synth.activations(rows, k, 8, "x")
+    b = synth.activations(1, n, 8, "b").reshape(-1)
+    out = torch.zeros(rows * n)
+    if pinned:
+        x, b, out = x.pin_memory(), b.pin_memory(), out.pin_memory()
+    backend.linear_out_by_in(x.numpy(), rows, k, w, n, b.numpy(), out.numpy())
+    ref = oracle.q_linear(12, blocks.numpy(), x.numpy(), rows, k, n, bias=b.numpy())
+    assert rel_err(out.numpy().reshape(rows, n), ref) <= GEMV_RTOL
+
+
+def test_unaligned_activation_rows(backend, oracle):
+    """x that starts 4 bytes past a 16-byte boundary (a view into a larger tensor)."""
+    from ocelotl_b200 import synth
+    n, k, rows = 256, 1024, 2
+    blocks = synth.quant_blocks(14, n, k, 4, "w")
+    w = backend.upload_quant(14, blocks, n, k)
+    xs = synth.activations(rows, k, 4, "x")
+    big = torch.zeros(rows * k + 1, device="cuda")
+    big[1:] = xs.reshape(-1).cuda()
+    x = big[1:]
+    assert x.data_ptr() % 16 == 4
+    for m in (1, rows):
+        y = torch.empty(m, n, device="cuda")
+        backend.linear_dev(w, x, m, y)
+        backend.synchronize()
+        ref = oracle.q_linear(14, blocks.numpy(), xs[:m].numpy(), m, k, n)
+        assert rel_err(y.cpu().numpy(), ref) <= GEMV_RTOL
