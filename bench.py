@@ -648,7 +648,8 @@ def run_ocelotl(args):
             "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "path": "CudaKernelBackend.linear_out_by_in -> ocl_q_linear_host per projection (pinned host "
-                            "x/y; copies, launches and a stream sync inside every call)"},
+                            "x/y, read and written by the kernels in place over the host link; launches and a "
+                            "stream sync inside every call)"},
             "gpu_launches": KERNELS_PER_CALL * len(LAYER) * args.steps,
             "device_errors": {"bad_ids": errs[0], "wait_timeouts": errs[1]},
             "clocks": clk,
