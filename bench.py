@@ -262,6 +262,10 @@ def run_stack(be, args, torch, synth, dev):
             blocks = synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.{name}", device=dev)
             ws[name] = be.upload_quant(t, blocks, n, k)
             del blocks
+        # the model path runs gate and up as one gated pass (ocelotl_b200/model.py)
+        ws["gate_up"] = be.pair_gated(ws["gate"], ws["up"])
+        ws.pop("gate").quant.free()
+        ws.pop("up").quant.free()
         layers.append(ws)
     head = be.upload_quant(Q6_K, synth.quant_blocks(Q6_K, vocab, HIDDEN, args.seed, "stack.head", device=dev),
                            vocab, HIDDEN)
@@ -278,11 +282,15 @@ def run_stack(be, args, torch, synth, dev):
         next_ids = torch.empty(m, dtype=torch.int32, device=dev)
         xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
 
+        act = torch.empty(m, FFN, device=dev)
+
         def token():
             be.embed_rows(emb, ids, h)
             for ws in layers:
-                for name, t, n, k, _ in LAYER:
-                    be.linear_dev(ws[name], xs[xin[name]], m, ys[name])
+                be.linear_dev(ws["qkv"], xs["qkv"], m, ys["qkv"])
+                be.linear_dev(ws["o"], xs["o"], m, ys["o"])
+                be.linear_gated(ws["gate_up"], xs["gate"], m, act)
+                be.linear_dev(ws["down"], xs["down"], m, ys["down"])
             be.linear_dev(head, h, m, logits)
             be.greedy_sample(logits, out=next_ids)
 
@@ -310,7 +318,8 @@ def run_stack(be, args, torch, synth, dev):
                        "head_argmax_us": round(head_us, 2),
                        "head_GB/s": round(wbytes(Q6_K, vocab, HIDDEN) / (head_us * 1e-6) / 1e9, 1)}
         del g
-    res["note"] = ("per decode step: Q8_0 embedding gather, 32 x (qkv, o, gate, up, down) quantized GEMVs and the "
+    res["note"] = ("per decode step: Q8_0 embedding gather, 32 x (qkv, o, gated gate+up pass, down) quantized GEMVs "
+                   "and the "
                    "Q6_K output head + greedy argmax over the 128256 logits, one CUDA graph; linear layers only (no attention "
                    "or norms); head_argmax_us = head GEMV + argmax alone")
     del layers, head, emb
