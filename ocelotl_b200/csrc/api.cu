@@ -216,7 +216,7 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
         const ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
-        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream), "x split launch");
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type), "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, pl, ctx->part,
                                   ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
@@ -236,7 +236,7 @@ int q_gated_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows,
         const ocl::GemvPlan pl = ocl::plan_gemv_gated(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
-        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream), "x split launch");
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type), "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv_gated(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, act + r0 * n, pl,
                                         ctx->part, ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
@@ -622,7 +622,7 @@ int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const
             return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: %d x %zu outputs (%lld CTAs) exceed the communicator "
                         "capacity (%lld elements, %lld groups)", m, n, (long long)pl.groups,
                         (long long)c->max_elems, (long long)c->max_groups);
-        OCL_CUDA(ctx, ocl::launch_xsplit(x_dev + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream),
+        OCL_CUDA(ctx, ocl::launch_xsplit(x_dev + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type),
                  "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias_dev, y_dev + r0 * n, pl,

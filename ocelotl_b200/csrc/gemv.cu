@@ -144,7 +144,10 @@ __device__ __forceinline__ int zext_byte(uint32_t w, int i) {
 // warp per (row m, 256-k block b).  Rows past `rows` up to mpad are written as
 // zeros (they feed idle MMA columns).  |x / xs| < 2^7 with xs = 2^e per block.
 // ---------------------------------------------------------------------------
-__global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, XPlanes p) {
+// `sums` selects which plane sums the GEMV that follows reads (bit 0 per-16
+// ints, 1 per-32 ints, 2 per-16 byte pieces, 3 per-32 byte pieces); the others
+// are not written.
+__global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, XPlanes p, int sums) {
     // Let the GEMV that follows launch now: it only streams weights until it
     // waits for this kernel.  This kernel itself must wait for its predecessor:
     // x is that kernel's output and the planes may still be read by it.
@@ -200,18 +203,22 @@ __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, 
         int s = sum[sp] + __shfl_xor_sync(0xffffffffu, sum[sp], 1);
         if ((lane & 1) == 0) {
             const int j = lane >> 1;
-            p.s16[(int64_t)c * (p.kx / 16) + b * 16 + j] = s;
-            int8_t* pc = p.p16 + ((int64_t)c * (p.kx / 256) + b) * 32;
-            pc[j] = (int8_t)(s & 63);        // s = lo + 64 * hi, lo in 0..63
-            pc[16 + j] = (int8_t)(s >> 6);   // |s| <= 2032 -> hi in -32..31
+            if (sums & 1) p.s16[(int64_t)c * (p.kx / 16) + b * 16 + j] = s;
+            if (sums & 4) {
+                int8_t* pc = p.p16 + ((int64_t)c * (p.kx / 256) + b) * 32;
+                pc[j] = (int8_t)(s & 63);        // s = lo + 64 * hi, lo in 0..63
+                pc[16 + j] = (int8_t)(s >> 6);   // |s| <= 2032 -> hi in -32..31
+            }
         }
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         if ((lane & 3) == 0) {
             const int j = lane >> 2;
-            p.s32[(int64_t)c * (p.kx / 32) + b * 8 + j] = s;
-            int8_t* pc = p.p32 + ((int64_t)c * (p.kx / 256) + b) * 16;
-            pc[j] = (int8_t)(s & 63);
-            pc[8 + j] = (int8_t)(s >> 6);    // |s| <= 4064 -> hi in -64..63
+            if (sums & 2) p.s32[(int64_t)c * (p.kx / 32) + b * 8 + j] = s;
+            if (sums & 8) {
+                int8_t* pc = p.p32 + ((int64_t)c * (p.kx / 256) + b) * 16;
+                pc[j] = (int8_t)(s & 63);
+                pc[8 + j] = (int8_t)(s >> 6);    // |s| <= 4064 -> hi in -64..63
+            }
         }
     }
     if (lane == 0)
@@ -1044,7 +1051,13 @@ XPlanes xplanes_carve(void* base, int64_t k) {
     return p;
 }
 
-cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s) {
+cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s,
+                          int type) {
+    // the sums the GEMV of `type` reads: byte pieces for a single row, ints otherwise
+    int sums = 15;
+    if (type == kQ4_K) sums = rows == 1 ? 8 : 2;
+    else if (type == kQ6_K) sums = rows == 1 ? 4 : 1;
+    else if (type == kQ8_0) sums = 0;
     const int nt = rows == 1 ? 0 : (3 * rows + 7) / 8;
     const int mpad = nt ? (nt * 8 + 2) / 3 : 1;  // activation rows whose planes the GEMV reads
     cudaLaunchConfig_t cfg = {};
@@ -1056,7 +1069,7 @@ cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, xsplit_kernel, x, rows, k, p);
+    return cudaLaunchKernelEx(&cfg, xsplit_kernel, x, rows, k, p, sums);
 }
 
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,

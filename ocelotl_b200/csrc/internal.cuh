@@ -46,7 +46,10 @@ cudaError_t launch_embed(const void* tiles, int64_t n_rows, int64_t k, const int
                          float* out, unsigned int* bad, cudaStream_t s);
 
 // x [rows<=16, k] f32 -> planes (waits for the previous kernel when `pdl`).
-cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s);
+// `type` (the GEMV's weight type) limits the plane sums written to the ones its
+// GEMV reads; -1 writes all of them.
+cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p, bool pdl, cudaStream_t s,
+                          int type = -1);
 
 // Launch geometry of one GEMV.
 struct GemvPlan {

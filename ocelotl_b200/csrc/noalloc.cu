@@ -122,7 +122,7 @@ extern "C" int ocl_q_linear_noalloc(int type, const void* w, size_t n_rows, size
     for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
         const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
         const ocl::GemvPlan pl = ocl::plan_gemv(type, (int64_t)n_rows, (int64_t)k, m, slot->sms);
-        e = ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, false, s);
+        e = ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, false, s, type);
         if (e == cudaSuccess)
             e = ocl::launch_gemv(type, w, (int64_t)n_rows, (int64_t)k, planes, m, bias, y + r0 * n_rows, pl, part,
                                  counters, flags, false, s);
