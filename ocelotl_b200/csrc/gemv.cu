@@ -797,10 +797,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
             }
             const uint8_t* rec = ring + st * UB;
             const int l = u0 + done - U0;
-#ifdef OCL_GEMV_PROBE_NOCOMPUTE
-            if (rec[lane] == 0xEE && l < 0) acc[0][0] += 1.f;  // data-movement ceiling experiment
-            else
-#endif
             if constexpr (NT == 0) {
                 if (TYPE == kQ4_K) consume_q4k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
                 else if (TYPE == kQ6_K) consume_q6k_m1(rec, l, X, acc[0][0], acc[0][2], g, t, lane);
