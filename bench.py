@@ -148,6 +148,18 @@ def cpu_layer_pass(oracle, weights, xs, m, threads):
     return time.perf_counter() - t0
 
 
+def host_info():
+    model = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu": model}
+
+
 def cpu_baseline(m, seed, budget_s=10.0):
     """Reference CPU path, one thread (the reference's dispatch is serial for rows < 32)."""
     import oracle
@@ -158,7 +170,7 @@ def cpu_baseline(m, seed, budget_s=10.0):
         spent += cpu_layer_pass(oracle, weights, xs, m, 1)
         passes += 1
     gbs = layer_alg_bytes(m) * passes / spent / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port", "host": host_info(),
             "sample": f"{passes} full layer passes (5 projections, M={m}) in {spent:.1f}s: GGUF dequant + "
                       f"sequential-k f32 linear_out_by_in (oracle/oracle.c), 1 thread"}
 
@@ -180,7 +192,7 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init GGUF blocks, N(0,1) activations)",
         "config": {"workload": WORKLOAD, "rows": args.rows, "host_threads": threads},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "host": host_info(),
                          "sample": f"each step = one full layer pass (M={args.rows}): GGUF dequant + sequential-k "
                                    f"f32 linear_out_by_in restated in C (oracle/), output features split over "
                                    f"{threads} threads (bit-identical to serial)"},
@@ -532,6 +544,17 @@ def run_ocelotl(args):
         dist.all_reduce(t_, op=dist.ReduceOp.MAX)
         ms = float(t_.item())
     ms_step = ms / args.steps
+    # spread of single steps, in a separate pass (an event between steps breaks
+    # the overlap of consecutive graphs, so it would slow the timed region)
+    n_dist = min(args.steps, 200)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_dist + 1)]
+    evs[0].record()
+    for i in range(n_dist):
+        run(i)
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    step_us = sorted(1e3 * evs[i].elapsed_time(evs[i + 1]) for i in range(n_dist))
+    pct = lambda q: round(step_us[min(len(step_us) - 1, int(q * len(step_us)))], 3)  # noqa: E731
     gbs = replicas * layer_alg_bytes(m) / (ms_step * 1e-3) / 1e9
 
     # ---- per-projection call time (split + GEMV), graphs of back-to-back calls
@@ -663,6 +686,7 @@ def run_ocelotl(args):
             "device_errors": {"bad_ids": errs[0], "wait_timeouts": errs[1]},
             "clocks": clk,
             "layer_us": round(ms_step * 1e3, 3),
+            "single_step_us_p10_p50_p90": [pct(0.1), pct(0.5), pct(0.9)],
             "decode_tok_s_layer": round(m / (ms_step * 1e-3), 1),
         }
         if sweep:
