@@ -1,6 +1,6 @@
 """Benchmark: Llama-3-8B-shaped decoder layer, all linear projections, GGUF-quantized.
 
-Workload: q/k/v fused 4096->6144, o 4096->4096, gate and up
+Workload (the headline: the 8B-shaped layer at decode batch M): q/k/v fused 4096->6144, o 4096->4096, gate and up
 4096->14336 each (Q4_K), down 14336->4096 (Q6_K); decode batch M (default 1),
 f32 activations N(0,1), seeded random-init weights (synthetic data generated on
 the device).  One step = one pass of the five projections, each its own
@@ -10,13 +10,14 @@ graph; weights rotate over enough distinct copies (>= 4x the 126 MB L2) that
 every step streams its weights from HBM.
 
 metric: algorithmic bytes (quantized weights + f32 activations in + outputs out)
-of the layer / time, GB/s.  With --gpus N (torchrun), by default every GPU
-runs the whole layer on its own decode batch (replicas: the 8B layer needs no
-exchange step; value = all GPUs' bytes / max-over-ranks time, weak scaling).
---mode tp splits the layer instead: q/k/v, gate, up by output rows, o and down
-by input columns with their outputs summed over ranks inside the GEMV (NVLink
-peer memory; NCCL with --nccl); total work fixed (strong scaling).  The
-70B-shaped layer is always timed tensor parallel over the N GPUs.
+of the layer / time, GB/s.  With --gpus N (torchrun), by default the layer is
+split over the N GPUs (tensor parallel, strong scaling: the total work is fixed):
+q/k/v, gate, up by output rows, o and down by input columns with their outputs
+summed over ranks inside the GEMV (NVLink peer memory; NCCL with --nccl).
+--mode replicas instead runs the whole layer on every GPU on its own decode
+batch (no exchange step; weak scaling); at N > 1 the replica figure is also
+reported beside the headline.  The 70B-shaped layer is always timed tensor
+parallel over the N GPUs.
 
 --impl reference times the reference's CPU algorithm (the C restatement in
 oracle/: GGUF dequant + sequential-k f32 linear_out_by_in) on the host cores.
@@ -75,17 +76,13 @@ def peaks():
 
 
 def profile_traffic(kernel_key):
-    """Per-launch DRAM bytes from the committed ncu summary (None if absent)."""
-    f = ROOT / "profiles" / "gemv_8b_layer_m1.md"
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of a
+    committed ncu capture, from profiles/dram_traffic.json (None if absent)."""
+    f = ROOT / "profiles" / "dram_traffic.json"
     if not f.exists():
         return None
-    for line in f.read_text().splitlines():
-        if line.startswith(f"dram_bytes_per_launch[{kernel_key}]:"):
-            try:
-                return int(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+    entry = json.loads(f.read_text()).get(kernel_key)
+    return None if entry is None else int(entry["dram_bytes_per_launch"])
 
 
 class Clocks:
@@ -141,11 +138,16 @@ def cpu_inputs(m, seed):
     return weights, xs
 
 
-def cpu_layer_pass(oracle, weights, xs, m, threads):
+def cpu_layer_pass(oracle, weights, xs, m, threads, avx2=False):
     t0 = time.perf_counter()
     for (name, t, n, k, _), blocks in zip(LAYER, weights):
-        oracle.q_linear(t, blocks, xs[name], m, k, n, threads=threads)
+        oracle.q_linear(t, blocks, xs[name], m, k, n, threads=threads, avx2=avx2)
     return time.perf_counter() - t0
+
+
+def has_avx2():
+    import oracle
+    return bool(oracle.lib().orc_has_avx2())
 
 
 def host_info():
@@ -161,18 +163,29 @@ def host_info():
 
 
 def cpu_baseline(m, seed, budget_s=10.0):
-    """Reference CPU path, one thread (the reference's dispatch is serial for rows < 32)."""
+    """Reference CPU path, one thread (the reference's dispatch is serial for rows < 32),
+    in both of its forms: the scalar linear_out_by_in and the AVX2 tile
+    (crates/kernels/src/cpu_avx2.rs:58-253), the reference's fastest CPU mode."""
     import oracle
     oracle.build()
     weights, xs = cpu_inputs(m, seed)
-    passes, spent = 0, 0.0
-    while spent < budget_s and passes < 50:
-        spent += cpu_layer_pass(oracle, weights, xs, m, 1)
-        passes += 1
-    gbs = layer_alg_bytes(m) * passes / spent / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port", "host": host_info(),
-            "sample": f"{passes} full layer passes (5 projections, M={m}) in {spent:.1f}s: GGUF dequant + "
-                      f"sequential-k f32 linear_out_by_in (oracle/oracle.c), 1 thread"}
+
+    def timed(avx2):
+        passes, spent = 0, 0.0
+        while spent < budget_s / 2 and passes < 50:
+            spent += cpu_layer_pass(oracle, weights, xs, m, 1, avx2=avx2)
+            passes += 1
+        return layer_alg_bytes(m) * passes / spent / 1e9, passes, spent
+    scalar, sp, ss = timed(False)
+    avx = has_avx2()
+    fast, fp, fs = timed(True) if avx else (None, 0, 0.0)
+    best = fast if fast is not None else scalar
+    return {"value": round(best, 3), "unit": "GB/s", "cores": 1, "kind": "port", "host": host_info(),
+            "isa": "avx2+fma" if avx else "scalar",
+            "scalar_GBs": round(scalar, 3), "avx2_GBs": None if fast is None else round(fast, 3),
+            "sample": f"full layer passes (5 projections, M={m}), 1 thread: GGUF dequant + linear_out_by_in restated "
+                      f"in C (oracle/oracle.c); scalar sequential-k: {sp} passes in {ss:.1f}s; AVX2 tile: "
+                      f"{fp} passes in {fs:.1f}s; value = the faster (AVX2 when the host has it)"}
 
 
 def run_reference(args):
@@ -181,10 +194,11 @@ def run_reference(args):
     import oracle
     oracle.build()
     threads = os.cpu_count() or 1
+    avx = has_avx2()
     weights, xs = cpu_inputs(args.rows, args.seed)
     for _ in range(args.warmup):
-        cpu_layer_pass(oracle, weights, xs, args.rows, threads)
-    total = sum(cpu_layer_pass(oracle, weights, xs, args.rows, threads) for _ in range(args.steps))
+        cpu_layer_pass(oracle, weights, xs, args.rows, threads, avx2=avx)
+    total = sum(cpu_layer_pass(oracle, weights, xs, args.rows, threads, avx2=avx) for _ in range(args.steps))
     gbs = layer_alg_bytes(args.rows) * args.steps / total / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
@@ -193,9 +207,10 @@ def run_reference(args):
         "data": "synthetic (seeded random-init GGUF blocks, N(0,1) activations)",
         "config": {"workload": WORKLOAD, "rows": args.rows, "host_threads": threads},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "host": host_info(),
-                         "sample": f"each step = one full layer pass (M={args.rows}): GGUF dequant + sequential-k "
-                                   f"f32 linear_out_by_in restated in C (oracle/), output features split over "
-                                   f"{threads} threads (bit-identical to serial)"},
+                         "isa": "avx2+fma" if avx else "scalar",
+                         "sample": f"each step = one full layer pass (M={args.rows}): GGUF dequant + "
+                                   f"linear_out_by_in ({'AVX2 tile, cpu_avx2.rs' if avx else 'scalar sequential-k'}) "
+                                   f"restated in C (oracle/), output features split over {threads} threads"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -221,6 +236,25 @@ def graph_of(fn, be, torch):
     return g
 
 
+def chain(be, torch, calls, pf):
+    """Run calls [(weight, fn)] in order on the current stream.  With a side
+    stream `pf`, the weight of call i + 1 is prefetched into L2 (ocl_q_prefetch_l2)
+    while call i runs: the prefetch waits for call i - 1, i.e. it starts when call
+    i does.  An entry with fn None is only prefetched (the next graph's first
+    weight).  The side stream joins the current one at the end."""
+    main = torch.cuda.current_stream()
+    for i, (w, fn) in enumerate(calls):
+        if pf is not None and i + 1 < len(calls):
+            ev = torch.cuda.Event()
+            ev.record(main)
+            pf.wait_event(ev)
+            be.prefetch_l2(calls[i + 1][0], pf)
+        if fn is not None:
+            fn()
+    if pf is not None:
+        main.wait_stream(pf)
+
+
 def bf16_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -229,7 +263,7 @@ def bf16_peak():
 
 
 def run_prefill(be, ws, sh, args, torch):
-    """the 8B layer's five projections as bf16 tcgen05 GEMMs, M = 512 and 2048 tokens."""
+    """Prefill: the 8B layer's five projections as bf16 tcgen05 GEMMs, M = 512 and 2048 tokens."""
     from ocelotl_b200 import synth
     out = {}
     peak, src = bf16_peak()
@@ -265,7 +299,7 @@ def run_prefill(be, ws, sh, args, torch):
 
 
 def run_stack(be, args, torch, synth, dev):
-    """32 decoder layers' projections + Q6_K output head + Q8_0 embedding rows, per decode token."""
+    """8B linear stack: 32 decoder layers' projections + Q6_K output head + Q8_0 embedding rows, per decode token."""
     n_layers, vocab = 32, 128256
     layers = []
     for li in range(n_layers):
@@ -349,7 +383,7 @@ LAYER_70B = [  # hidden 8192, GQA kv 1024 (q 8192 + k 1024 + v 1024), ffn 28672
 
 
 def run_tp70b(be, args, torch, synth, dev, rank, tp, comm, group):
-    """one Llama-3-70B-shaped layer's projections under tensor parallelism (per decode token)."""
+    """70B-shaped layer's projections under tensor parallelism (per decode token)."""
     from ocelotl_b200.tp import TPLinear
     import torch.distributed as dist
     shards = [(nm, t, n // tp, k, sp) if sp == "col" else (nm, t, n, k // tp, sp) for nm, t, n, k, sp in LAYER_70B]
@@ -413,6 +447,82 @@ def time_graphs(gs, n_it, torch):
     b.record()
     torch.cuda.synchronize()
     return 1e3 * a.elapsed_time(b) / n_it
+
+
+def run_replicas(be, args, torch, synth, dev, rank, world):
+    """Every GPU runs the whole 8B layer on its own decode batch (no exchange
+    step): value = all GPUs' algorithmic bytes / max-over-ranks time (weak scaling)."""
+    import torch.distributed as dist
+    m = args.rows
+    layer_w = sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER)
+    copies = max(2, -(-4 * L2_BYTES // layer_w))
+    weights = [{nm: be.upload_quant(t, synth.quant_blocks(t, n, k, args.seed, f"rep.{nm}.r{rank}.c{c}", device=dev),
+                                    n, k) for nm, t, n, k, _ in LAYER} for c in range(copies)]
+    xs = {nm: synth.activations(m, k, args.seed, f"rep.x.{nm}.r{rank}", device=dev) for nm, t, n, k, _ in LAYER}
+    ys = {nm: torch.empty(m, n, device=dev) for nm, t, n, k, _ in LAYER}
+    xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+    gs = [graph_of(lambda c=c: [be.linear_dev(weights[c][nm], xs[xin[nm]], m, ys[nm]) for nm, *_ in LAYER],
+                   be, torch) for c in range(copies)]
+    for i in range(3):
+        gs[i % copies].replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(args.steps):
+        gs[i % copies].replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = 1e3 * a.elapsed_time(b) / args.steps
+    if world > 1:
+        t_ = torch.tensor([us])
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        us = float(t_.item())
+    del gs, weights
+    torch.cuda.synchronize()
+    return {"value": round(world * layer_alg_bytes(m) / (us * 1e-6) / 1e9, 2), "unit": "GB/s", "layer_us": round(us, 3),
+            "decode_tok_s": round(world * m / (us * 1e-6), 1), "scaling": "weak",
+            "note": f"{world} independent full layers, one per GPU, max-over-ranks time"}
+
+
+SINGLE_GEMVS = [  # (key, type, out_features, in_features)
+    ("q4k_4096x4096", Q4_K, 4096, 4096),     # the single Q4_K dequant + matvec case
+    ("q4k_14336x4096", Q4_K, 14336, 4096),   # the 8B gate / up shape
+    ("q4k_4096x14336", Q4_K, 4096, 14336),   # Q4_K with the down projection's long K
+    ("q6k_4096x14336", Q6_K, 4096, 14336),   # the 8B down projection
+]
+
+
+def run_single_gemvs(be, args, torch, synth, dev, peak, pf=None):
+    """Back-to-back calls of one GEMV shape at M = 1 over distinct weight copies
+    (>= 4x L2 together, so every call streams from HBM), in a CUDA graph."""
+    out = {}
+    for key, t, n, k in SINGLE_GEMVS:
+        copies = max(4, -(-4 * L2_BYTES // wbytes(t, n, k)))
+        ws = [be.upload_quant(t, synth.quant_blocks(t, n, k, args.seed, f"single.{key}.{c}", device=dev), n, k)
+              for c in range(copies)]
+        x = synth.activations(1, k, args.seed, f"single.x.{key}", device=dev)
+        y = torch.empty(1, n, device=dev)
+        g = graph_of(lambda: [be.linear_dev(w, x, 1, y) for w in ws], be, torch)
+        us = time_graphs([g], max(10, args.steps // 10), torch) / copies
+        b = proj_bytes(t, n, k, 1)
+        gbs = b / (us * 1e-6) / 1e9
+        out[key] = {"us": round(us, 3), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes": b,
+                    "copies": copies}
+        if pf is not None:  # the same calls with the next copy prefetched into L2 during each call
+            calls = [(w, lambda w=w: be.linear_dev(w, x, 1, y)) for w in ws] + [(ws[0], None)]
+            g2 = graph_of(lambda: chain(be, torch, calls, pf), be, torch)
+            us2 = time_graphs([g2], max(10, args.steps // 10), torch) / copies
+            gbs2 = b / (us2 * 1e-6) / 1e9
+            out[key].update({"us_prefetch": round(us2, 3), "GB/s_prefetch": round(gbs2, 1),
+                             "frac_prefetch": round(gbs2 / peak, 4)})
+            del g2
+        del g
+        for w in ws:
+            w.quant.free()
+    torch.cuda.synchronize()
+    return out
 
 
 def run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev):
@@ -508,10 +618,14 @@ def run_ocelotl(args):
     ys = {name: torch.empty(m, n, device=dev, dtype=torch.float32) for name, t, n, k, _ in shards}
     xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
 
+    pf = torch.cuda.Stream(device=dev) if args.prefetch else None
+
     def step(c):
         ws = weights[c]
-        for name, t, n, k, sp in shards:
-            ws[name].forward(xs[xin[name]], m, ys[name])
+        calls = [(ws[name].weight, lambda name=name: ws[name].forward(xs[xin[name]], m, ys[name]))
+                 for name, *_ in shards]
+        calls.append((weights[(c + 1) % copies][shards[0][0]].weight, None))
+        chain(be, torch, calls, pf)
 
     # ---- device-resident timing: one graph per weight copy --------------------
     if tp > 1:
@@ -622,7 +736,7 @@ def run_ocelotl(args):
         e2e_s = float(t_.item())
     e2e_gbs = replicas * layer_alg_bytes(m) * args.steps / e2e_s / 1e9
 
-    # ---- decode batch sweep (configs[1]: M = 1, 2, 4, 8, 16), graphs ----------
+    # ---- decode batch sweep (M = 1, 2, 4, 8, 16), graphs ----------------------
     sweep = {}
     if args.sweep and tp == 1:
         for mm in (1, 2, 4, 8, 16):
@@ -648,13 +762,34 @@ def run_ocelotl(args):
                               "tok_s_layer": round(mm / (us * 1e-6), 1)}
             del gs
 
+    errs_seen = {"bad_ids": 0, "wait_timeouts": 0}
+    bad_sections = []
+
+    def check(section):
+        """Device errors of the section just timed; its figures are void if a wait gave up."""
+        b, tmo = be.take_device_errors()
+        errs_seen["bad_ids"] += b
+        errs_seen["wait_timeouts"] += tmo
+        if tmo:
+            bad_sections.append(section)
+        return tmo == 0
+    layer_ok = check("layer")
+    peak_gbs, _ = peaks()
+    single = run_single_gemvs(be, args, torch, synth, dev, peak_gbs, pf) if (args.single and tp == 1) else None
+    if single is not None and not check("single_gemvs"):
+        single = None
     fused = run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev) if (args.fused_mlp and tp == 1) \
         else None
     tp70 = run_tp70b(be, args, torch, synth, dev, rank, world, comm, nccl() if world > 1 else None) \
         if args.tp70b else None
     prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
+    if tp70 is not None and not check("tp_70b_layer"):
+        tp70 = {"error": "device waits timed out; figures void", "wait_timeouts": errs_seen["wait_timeouts"]}
     stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
-    errs = be.take_device_errors()
+    reps = run_replicas(be, args, torch, synth, dev, rank, world) if (world > 1 and tp > 1 and args.replicas) \
+        else None
+    check("rest")
+    errs = (errs_seen["bad_ids"], errs_seen["wait_timeouts"])
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(m, args.seed, budget_s=args.cpu_budget)
@@ -699,6 +834,17 @@ def run_ocelotl(args):
             line["tp_70b_layer"] = tp70
         if stack:
             line["linear_stack_8b"] = stack
+        if single:
+            line["single_gemv_m1"] = single
+        if reps:
+            line["replicas"] = reps
+        if not layer_ok or bad_sections:
+            # a bounded device wait gave up: outputs were left unwritten, so the
+            # timings do not measure the work; report nothing as a value
+            line["error"] = f"device waits timed out in {bad_sections}; values void"
+            if not layer_ok:
+                line["value"] = None
+                line["e2e"]["value"] = None
         print(json.dumps(line), flush=True)
     if world > 1:
         # Leave without tearing the process group down: graphs captured with
@@ -708,8 +854,8 @@ def run_ocelotl(args):
         dist.barrier()
         sys.stdout.flush()
         sys.stderr.flush()
-        os._exit(0)
-    return 0
+        os._exit(0 if errs[1] == 0 else 1)
+    return 0 if errs[1] == 0 else 1
 
 
 def run_profile_case(args):
@@ -757,15 +903,20 @@ def main():
     ap.add_argument("--seed", type=int, default=0x0CE107)
     ap.add_argument("--sweep", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["replicas", "tp"], default="replicas",
-                    help="N > 1: independent full layers per GPU (weak scaling) or one layer split over the GPUs")
+    ap.add_argument("--mode", choices=["replicas", "tp"], default="tp",
+                    help="N > 1: one layer split over the GPUs (strong scaling, default) or independent full layers "
+                         "per GPU (weak scaling)")
+    ap.add_argument("--replicas", type=int, default=1, help="N > 1 in tp mode: also time N independent replicas")
     ap.add_argument("--nccl", action="store_true", help="TP: NCCL all-reduce instead of the fused one")
-    ap.add_argument("--tp70b", type=int, default=1, help="also time configs[4] (70B-shaped layer, TP = N)")
-    ap.add_argument("--prefill", type=int, default=1, help="also time configs[2] (bf16 tcgen05 GEMM)")
-    ap.add_argument("--stack", type=int, default=1, help="also time configs[3] (8B linear stack per token)")
+    ap.add_argument("--tp70b", type=int, default=1, help="also time the 70B-shaped layer (TP = N)")
+    ap.add_argument("--prefill", type=int, default=1, help="also time the prefill GEMM (bf16 tcgen05, M = 512 / 2048)")
+    ap.add_argument("--stack", type=int, default=1, help="also time the 8B linear stack per decode token")
     ap.add_argument("--fused-mlp", type=int, default=1,
                     help="also time the layer with gate+up as one fused gated pass (ocl_q_linear_gated)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--single", type=int, default=1, help="also time single GEMV shapes at M = 1")
+    ap.add_argument("--prefetch", type=int, default=1,
+                    help="prefetch the next projection's weight into L2 on a side stream (ocl_q_prefetch_l2)")
     ap.add_argument("--case", choices=["gemv", "gemm"], help="run a small profiling case instead of the bench")
     ap.add_argument("--case-shape", default="12:14336:4096")
     args = ap.parse_args()

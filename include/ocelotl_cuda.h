@@ -84,6 +84,10 @@ OCL_API int ocl_synchronize(ocl_ctx* ctx);
  * stream starts while the previous kernel on the stream finishes; it reads its
  * activations only after that kernel completed. */
 OCL_API int ocl_set_pdl(ocl_ctx* ctx, int enable);
+/* Rows at which ocl_q_linear / ocl_q_linear_host / the gated calls switch
+ * from the GEMV to the bf16 tcgen05 GEMM (default 64; 0 = always the GEMV,
+ * keeping the 1e-3 GEMV accuracy at any rows). */
+OCL_API int ocl_set_gemm_min_rows(ocl_ctx* ctx, size_t rows);
 /* Backend id used in KernelError{backend}: "cuda-sm100a". */
 OCL_API const char* ocl_backend_id(void);
 OCL_API int ocl_abi_version(void);
@@ -123,16 +127,28 @@ OCL_API int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_bloc
  * k == in_features.  Replaces KernelBackend::linear_d for a quantized weight
  * (crates/kernels/src/lib.rs:193-217) and, via ocl_q_linear_host, the slice form
  * linear_out_by_in (crates/kernels/src/lib.rs:107-116, 1939-1967).
- * rows 1..16 run the dequant-GEMV (HBM-bound); larger `rows` are processed in
- * 16-row groups by the same kernel.  Accuracy: the products of the integer
- * quants with x are computed exactly (x split into three int8 planes per 256-k
- * block, i.e. ~21 significant bits), scaled and accumulated in f32; max relative
- * error vs the f32 CPU oracle <= 1e-3. */
+ * rows 1..16 run the dequant-GEMV (HBM-bound); rows below the context's GEMM
+ * threshold (64 by default, ocl_set_gemm_min_rows) are processed in 16-row
+ * groups by the same kernel.  GEMV accuracy: the products of the integer quants
+ * with x are computed exactly (x split into three int8 planes per 256-k block,
+ * i.e. ~21 significant bits), scaled and accumulated in f32; max relative error
+ * vs the f32 CPU oracle <= 1e-3.
+ * rows >= the threshold (prefill, e.g. Whisper's encoder at rows = audio_ctx,
+ * crates/models/src/whisper/primitives.rs:787-839) with in_features a multiple
+ * of 256 run ONE tcgen05 GEMM instead, so the weight is streamed once: x is
+ * rounded to bf16 on the device, the weight tiles are dequantized to bf16, the
+ * products accumulate in f32 and y (+ bias) is written in f32.  Accuracy then:
+ * max |y - r| / max(|r|, rms(r)) <= 2e-2 vs the f32 oracle on the bf16-rounded
+ * x, the prefill bound.  The bf16 copy of x lives in a context buffer grown on
+ * demand (rows * in_features * 2 bytes). */
 OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, size_t rows,
                  size_t in_features, size_t out_features, const float* bias_dev, float* y_dev);
 
 /* Same with host buffers (x, bias, y in host memory), on the context stream,
  * synchronising before it returns.  The slice-based linear_out_by_in.
+ * Returns OCL_ERR_TIMEOUT (KernelError) when a bounded device wait gave up
+ * during the call, or in an earlier device-pointer call of this context that
+ * ocl_take_device_errors has not reported yet; the counter is then cleared.
  * Page-locked (pinned) buffers are read and written by the kernels in place
  * through unified addressing; pageable ones are copied through a device staging
  * area kept by the context.  (Environment OCL_HOST_ZEROCOPY=0 forces staging.) */
@@ -154,12 +170,19 @@ OCL_API int ocl_tp_comm_create(ocl_ctx* ctx, int rank, int world, size_t max_ele
                                ocl_tpcomm** out, void* ipc_handle_out);
 OCL_API int ocl_tp_comm_open(ocl_ctx* ctx, ocl_tpcomm* comm, const void* ipc_handles);
 OCL_API int ocl_tp_comm_destroy(ocl_tpcomm* comm);
+/* Device address of this rank's arrival flags, u32 [world][max_groups]: slot
+ * [p][g] holds the launch tag rank p last stored for row group g.  For tests of
+ * the flag protocol (e.g. a peer that is already one launch ahead). */
+OCL_API unsigned int* ocl_tp_comm_flags(ocl_tpcomm* comm);
 /* Row-split quantized linear with the all-reduce fused into the GEMV: each rank
  * holds W[:, k0:k1] and x[:, k0:k1]; every rank's y receives the sum over ranks
  * (plus bias), identical bits on every rank.  Each CTA pushes its rows to every
  * peer, signals a per-row-group flag and waits (bounded, ~1 s; a timeout is
  * counted by ocl_take_device_errors and leaves y unwritten) for the peers'
  * rows.  Every rank must issue the same sequence of these calls. */
+/* Flag protocol: launch e stores tag e + 1; a waiter accepts any tag at or past
+ * its own, because a peer that finished launch e may already have stored tag
+ * e + 2 into the same single slot. */
 OCL_API int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* comm, const ocl_qbuf* w, const float* x_dev,
                                    size_t rows, size_t in_features, size_t out_features, const float* bias_dev,
                                    float* y_dev);
@@ -180,11 +203,30 @@ OCL_API int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* comm, const ocl_qbu
  * that array's device address (no allocation); make the first call before any
  * stream capture.  All calls share the array, so calls that overlap on the GPU
  * (different streams or devices' contexts racing on one device) race on it:
- * serialise them on one stream.  Results equal ocl_q_linear's.  Errors:
- * ocl_last_error(NULL). */
+ * serialise them on one stream.  `stream` must belong to the current device
+ * (OCL_ERR_INVALID otherwise).  Results are bit-identical to ocl_q_linear's
+ * for rows <= 16 per launch (same kernels, same plan).  Errors:
+ * ocl_last_error(NULL).  A bounded device wait that gives up is counted in the
+ * same array; read it with ocl_noalloc_take_device_errors. */
 OCL_API int ocl_q_linear_noalloc(int ggml_type, const void* w_tiled_dev, size_t n_rows, size_t k,
                                  const float* x_dev, size_t rows, const float* bias_dev, float* y_dev,
                                  void* stream);
+/* Read and clear the wait-timeout counter that ocl_q_linear_noalloc calls on
+ * the current device accumulate (a copy on `stream`, then a stream
+ * synchronisation; no allocation).  Returns OCL_ERR_TIMEOUT when it was
+ * non-zero. */
+OCL_API int ocl_noalloc_take_device_errors(void* stream, unsigned int* timeouts);
+
+/* Pull weight `w` into L2 ahead of the call that reads it, on `stream`
+ * (cudaStream_t; normally a side stream, since on the stream of the GEMVs it
+ * would only run between them).  A decode step is a chain of dependent GEMVs,
+ * and between one call finishing and the next one streaming (activation split,
+ * kernel hand-off) HBM sits idle; prefetching the NEXT projection's weight
+ * while the current one runs fills that gap, and the GEMV then reads its
+ * records from L2.  A hint only: no result changes, no ordering against other
+ * work is needed, and a weight evicted before use is read from HBM as usual.
+ * Keep at most the next one or two weights in flight (L2 is 126 MB). */
+OCL_API int ocl_q_prefetch_l2(ocl_ctx* ctx, const ocl_qbuf* w, void* stream);
 
 /* Prefill: y bf16 [rows, out_features] = x bf16 [rows, in_features] . W^T, f32
  * accumulate on tcgen05 tensor cores (weights dequantized to bf16 tiles in
@@ -241,8 +283,12 @@ OCL_API int ocl_q_embed_rows(ocl_ctx* ctx, const ocl_qbuf* table, const int32_t*
                      float* out_dev);
 /* Read and clear the context's device-side error counters (synchronises the
  * stream): embedding ids that were out of range, and bounded device waits that
- * gave up (a GEMV whose shared-memory stream stalled for ~1 s; its output is
- * then invalid).  Either pointer may be NULL. */
+ * gave up (a GEMV whose shared-memory stream stalled for ~1 s, or a fused
+ * all-reduce whose peers did not signal in ~1 s; that output is then
+ * incomplete).  Either pointer may be NULL.  Returns OCL_ERR_TIMEOUT (after
+ * filling both counters) when any wait gave up, so that a caller checking only
+ * the status still sees the failure (KernelError in the reference's terms,
+ * crates/core/src/lib.rs:75-80). */
 OCL_API int ocl_take_device_errors(ocl_ctx* ctx, unsigned int* bad_ids, unsigned int* timeouts);
 
 #ifdef __cplusplus

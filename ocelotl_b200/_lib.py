@@ -29,6 +29,8 @@ SIGNATURES = {
     "ocl_set_stream": (C.c_int, [_vp, _vp]),
     "ocl_synchronize": (C.c_int, [_vp]),
     "ocl_set_pdl": (C.c_int, [_vp, C.c_int]),
+    "ocl_set_gemm_min_rows": (C.c_int, [_vp, _sz]),
+    "ocl_q_prefetch_l2": (C.c_int, [_vp, _vp, _vp]),
     "ocl_backend_id": (C.c_char_p, []),
     "ocl_abi_version": (C.c_int, []),
     "ocl_q_upload": (C.c_int, [_vp, C.c_int, _vp, _sz, _sz, C.c_int, C.POINTER(_vp)]),
@@ -43,6 +45,8 @@ SIGNATURES = {
     "ocl_tp_comm_create": (C.c_int, [_vp, C.c_int, C.c_int, _sz, _sz, C.POINTER(_vp), _vp]),
     "ocl_tp_comm_open": (C.c_int, [_vp, _vp, _vp]),
     "ocl_tp_comm_destroy": (C.c_int, [_vp]),
+    "ocl_tp_comm_flags": (_vp, [_vp]),
+    "ocl_noalloc_take_device_errors": (C.c_int, [_vp, C.POINTER(C.c_uint)]),
     "ocl_q_linear_allreduce": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_linear_host": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_gemm_bf16": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),

@@ -304,10 +304,21 @@ class CudaKernelBackend:
         return out
 
     def take_device_errors(self) -> tuple[int, int]:
-        """(out-of-range embedding ids, device waits that timed out) since the last call."""
+        """(out-of-range embedding ids, device waits that timed out) since the last call.
+
+        The C call also returns OCL_ERR_TIMEOUT when waits timed out; here the
+        counts are returned either way (check_device_errors raises instead).
+        """
+        bad, tmo = C.c_uint(), C.c_uint()
+        rc = self._lib.ocl_take_device_errors(self._ctx, C.byref(bad), C.byref(tmo))
+        if rc != _lib.OCL_ERR_TIMEOUT:
+            self._check(rc)
+        return bad.value, tmo.value
+
+    def check_device_errors(self) -> None:
+        """Raise KernelError if a bounded device wait gave up since the last check."""
         bad, tmo = C.c_uint(), C.c_uint()
         self._check(self._lib.ocl_take_device_errors(self._ctx, C.byref(bad), C.byref(tmo)))
-        return bad.value, tmo.value
 
     def take_bad_ids(self) -> int:
         return self.take_device_errors()[0]
@@ -319,6 +330,15 @@ class CudaKernelBackend:
         self._check(self._lib.ocl_q_linear_allreduce(
             self._ctx, comm.handle, w.handle, C.c_void_p(x.data_ptr()), rows, w.k, w.n_rows,
             C.c_void_p(bias.data_ptr()) if bias is not None else None, C.c_void_p(out.data_ptr())))
+
+    def prefetch_l2(self, weight, stream: torch.cuda.Stream | None = None) -> None:
+        """Hint: pull a weight into L2 on `stream` (a side stream) before the call that reads it."""
+        w = self._quant_weight(weight)
+        self._check(self._lib.ocl_q_prefetch_l2(self._ctx, w.handle, C.c_void_p(stream.cuda_stream if stream else 0)))
+
+    def set_gemm_min_rows(self, rows: int) -> None:
+        """Rows at which linear_d switches to the bf16 tcgen05 GEMM (2e-2 bound); 0 = never."""
+        self._check(self._lib.ocl_set_gemm_min_rows(self._ctx, rows))
 
     def set_pdl(self, enable: bool) -> None:
         self._check(self._lib.ocl_set_pdl(self._ctx, 1 if enable else 0))

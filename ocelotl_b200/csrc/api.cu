@@ -32,6 +32,10 @@ struct ocl_ctx {
     size_t counter_count = 0;
     bool pdl = true;  // launch with programmatic dependent launch
     unsigned int* dev_flags = nullptr;  // [0] bad embedding ids, [1] bounded waits that gave up
+    unsigned int* host_flags = nullptr;  // pinned: the host-slice call's copy of dev_flags[1]
+    uint16_t* xbf = nullptr;  // bf16 copy of x for the prefill GEMM form, grown on demand
+    size_t xbf_bytes = 0;
+    size_t gemm_min_rows = 64;  // rows at which ocl_q_linear switches to the tcgen05 GEMM (0 = never)
 };
 
 struct ocl_tpcomm {
@@ -205,9 +209,43 @@ int check_linear_shapes(ocl_ctx* ctx, const ocl_qbuf* w, size_t rows, size_t in_
     return OCL_OK;
 }
 
+int ensure_xbf(ocl_ctx* ctx, size_t bytes) {
+    if (ctx->xbf_bytes >= bytes) return OCL_OK;
+    if (ctx->xbf) {
+        OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        cudaFree(ctx->xbf);
+        ctx->xbf = nullptr;
+        ctx->xbf_bytes = 0;
+    }
+    OCL_CUDA(ctx, cudaMalloc((void**)&ctx->xbf, bytes), "cudaMalloc(bf16 activations)");
+    ctx->xbf_bytes = bytes;
+    return OCL_OK;
+}
+
+// Many rows (prefill): one tcgen05 GEMM over bf16-rounded x instead of
+// rows/16 GEMV passes that would each stream the whole weight.
+bool use_gemm(const ocl_ctx* ctx, const ocl_qbuf* w, size_t rows) {
+    return ctx->gemm_min_rows > 0 && rows >= ctx->gemm_min_rows && w->k % 256 == 0;
+}
+
+int q_gemm_f32_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, const float* bias, float* y,
+                      bool gated) {
+    const size_t k = w->k, n = w->n_rows;
+    int rc = ensure_xbf(ctx, rows * k * 2 + 256);
+    if (rc) return rc;
+    OCL_CUDA(ctx, ocl::launch_cast_bf16(x, ctx->xbf, (int64_t)(rows * k), ctx->stream), "bf16 cast launch");
+    const int64_t n_gemm = gated ? (int64_t)((n + 15) / 16) * 32 : (int64_t)n;
+    OCL_CUDA(ctx,
+             ocl::launch_qgemm(w->type, w->dev, (int64_t)rows, n_gemm, (int64_t)k, ctx->xbf, nullptr, ctx->dev_flags,
+                               ctx->stream, gated ? (int64_t)n : 0, y, bias),
+             "prefill gemm launch");
+    return OCL_OK;
+}
+
 // y = x . W^T (+bias) for device pointers, any rows (16-row groups).
 int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, const float* bias, float* y) {
     const size_t k = w->k, n = w->n_rows;
+    if (use_gemm(ctx, w, rows)) return q_gemm_f32_locked(ctx, w, x, rows, bias, y, false);
     int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
     if (rc) return rc;
     const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
@@ -216,7 +254,8 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
         const ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
-        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type), "x split launch");
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type),
+                 "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, pl, ctx->part,
                                   ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
@@ -228,15 +267,17 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
 // act [rows, n_gate] = silu(x . Wg^T) * (x . Wu^T) over an interleaved pair.
 int q_gated_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, float* act) {
     const size_t k = w->k, n = w->n_rows;
+    if (use_gemm(ctx, w, rows)) return q_gemm_f32_locked(ctx, w, x, rows, nullptr, act, true);
     int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
     if (rc) return rc;
-    ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
+    const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
     for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
         const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
         const ocl::GemvPlan pl = ocl::plan_gemv_gated(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
-        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type), "x split launch");
+        OCL_CUDA(ctx, ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type),
+                 "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv_gated(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, act + r0 * n, pl,
                                         ctx->part, ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
@@ -261,6 +302,19 @@ int check_gated_shapes(ocl_ctx* ctx, const ocl_qbuf* gu, size_t rows, size_t hid
         return fail(ctx, OCL_ERR_INVALID, "mlp_gated_silu gate_w out_features=%zu does not match intermediate=%zu",
                     gu->n_rows, intermediate);
     return OCL_OK;
+}
+
+// A kernel of this call (or an earlier device-pointer call not yet checked)
+// gave up a bounded wait: clear the counter and report it as KernelError.
+int take_timeouts(ocl_ctx* ctx, const char* op) {
+    const unsigned int n = ctx->host_flags[0];
+    ctx->host_flags[0] = 0;
+    cudaError_t e = cudaMemsetAsync(ctx->dev_flags + 1, 0, 4, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "clear timeout counter");
+    return fail(ctx, OCL_ERR_TIMEOUT,
+                "%s: %u bounded device wait(s) gave up (~1 s each); the output of the affected row groups is "
+                "incomplete", op, n);
 }
 
 }  // namespace
@@ -296,7 +350,9 @@ int ocl_cuda_init(int device, ocl_ctx** out) {
     ctx->sms = prop.multiProcessorCount;
     e = cudaMalloc(&ctx->dev_flags, 64);
     if (e == cudaSuccess) e = cudaMemset(ctx->dev_flags, 0, 64);
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&ctx->host_flags, 64, cudaHostAllocDefault);
     if (e != cudaSuccess) {
+        if (ctx->dev_flags) cudaFree(ctx->dev_flags);
         delete ctx;
         return cuda_fail(nullptr, e, "context allocation");
     }
@@ -316,6 +372,8 @@ void ocl_cuda_destroy(ocl_ctx* ctx) {
         if (ctx->part) cudaFree(ctx->part);
         if (ctx->counters) cudaFree(ctx->counters);
         if (ctx->dev_flags) cudaFree(ctx->dev_flags);
+        if (ctx->host_flags) cudaFreeHost(ctx->host_flags);
+        if (ctx->xbf) cudaFree(ctx->xbf);
     }
     delete ctx;
 }
@@ -486,10 +544,14 @@ int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size
     if (e == cudaSuccess) {
         rc = q_linear_locked(ctx, w, xd, rows, bd, yd);
         if (rc == OCL_OK && !y_mapped) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
+        // the bounded-wait counter rides along with the result (one synchronisation)
+        if (rc == OCL_OK && e == cudaSuccess)
+            e = cudaMemcpyAsync(ctx->host_flags, ctx->dev_flags + 1, 4, cudaMemcpyDeviceToHost, ctx->stream);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(ctx, e, "linear_out_by_in host path");
+    if (ctx->host_flags[0] != 0) return take_timeouts(ctx, "linear_out_by_in");
     return OCL_OK;
 }
 
@@ -519,6 +581,10 @@ int ocl_take_device_errors(ocl_ctx* ctx, unsigned int* bad_ids, unsigned int* ti
     OCL_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     if (bad_ids) *bad_ids = h[0];
     if (timeouts) *timeouts = h[1];
+    if (h[1] != 0)
+        return fail(ctx, OCL_ERR_TIMEOUT,
+                    "%u bounded device wait(s) gave up since the last check (~1 s each); the outputs of the "
+                    "affected launches are incomplete", h[1]);
     return OCL_OK;
 }
 
@@ -585,6 +651,11 @@ int ocl_tp_comm_destroy(ocl_tpcomm* c) {
     if (c->buf) cudaFree(c->buf);
     delete c;
     return OCL_OK;
+}
+
+unsigned int* ocl_tp_comm_flags(ocl_tpcomm* c) {
+    if (!c || !c->buf) return nullptr;
+    return reinterpret_cast<unsigned int*>(static_cast<char*>(c->buf) + (size_t)2 * c->world * c->max_elems * 4);
 }
 
 int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const float* x_dev, size_t rows,
@@ -707,6 +778,26 @@ int ocl_q_mlp_gated_silu(ocl_ctx* ctx, const ocl_qbuf* gate_up, const ocl_qbuf* 
     rc = q_gated_locked(ctx, gate_up, x_dev, rows, act_dev);
     if (rc) return rc;
     return q_linear_locked(ctx, down, act_dev, rows, nullptr, out_dev);
+}
+
+int ocl_q_prefetch_l2(ocl_ctx* ctx, const ocl_qbuf* w, void* stream) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!w) return fail(ctx, OCL_ERR_INVALID, "prefetch_l2: weight is null");
+    if (w->device != ctx->device)
+        return fail(ctx, OCL_ERR_INVALID, "weight lives on device %d but the context is on device %d", w->device,
+                    ctx->device);
+    DeviceGuard guard(ctx->device);
+    OCL_CUDA(ctx, ocl::launch_prefetch_l2(w->dev, (uint64_t)w->bytes, static_cast<cudaStream_t>(stream)),
+             "prefetch_l2 launch");
+    return OCL_OK;
+}
+
+int ocl_set_gemm_min_rows(ocl_ctx* ctx, size_t rows) {
+    if (!ctx) return OCL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->gemm_min_rows = rows;
+    return OCL_OK;
 }
 
 int ocl_set_pdl(ocl_ctx* ctx, int enable) {

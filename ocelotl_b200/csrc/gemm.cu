@@ -267,7 +267,8 @@ __device__ __forceinline__ void dequant_quarter(const UnitRegs& R, int qt, int r
 template <int TYPE, bool GATED, int STAGES>
 __global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, int64_t M, int64_t N,
-                 int64_t K, uint16_t* __restrict__ y, int64_t n_out, unsigned int* __restrict__ err) {
+                 int64_t K, uint16_t* __restrict__ y, int64_t n_out, unsigned int* __restrict__ err,
+                 float* __restrict__ yf, const float* __restrict__ bias) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -394,7 +395,20 @@ __global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
                       "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
                     : "r"(taddr));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (m < M && GATED) {
+                if (m < M && GATED && yf) {
+                    float p[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) p[i] = silu_mul(__uint_as_float(v[i]), __uint_as_float(v[16 + i]));
+                    const int64_t n = (n0 + c0) / 2;
+                    float* dst = yf + m * n_out + n;
+                    if (n + 16 <= n_out && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            reinterpret_cast<float4*>(dst)[i] = make_float4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+                    } else {
+                        for (int i = 0; i < 16 && n + i < n_out; ++i) dst[i] = p[i];
+                    }
+                } else if (m < M && GATED) {
                     uint32_t p[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
@@ -408,6 +422,21 @@ __global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
                     } else {
                         for (int i = 0; i < 16 && n + i < n_out; ++i)
                             dst[i] = (uint16_t)(i & 1 ? p[i >> 1] >> 16 : p[i >> 1] & 0xffffu);
+                    }
+                } else if (m < M && yf) {
+                    // f32 output (+ bias): the linear_d form of the prefill GEMM
+                    float p[32];
+                    const int64_t n = n0 + c0;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        p[i] = __uint_as_float(v[i]) + ((bias && n + i < N) ? __ldg(bias + n + i) : 0.0f);
+                    float* dst = yf + m * N + n;
+                    if (n + 32 <= N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            reinterpret_cast<float4*>(dst)[i] = make_float4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+                    } else {
+                        for (int i = 0; i < 32 && n + i < N; ++i) dst[i] = p[i];
                     }
                 } else if (m < M) {
                     uint32_t p[16];
@@ -455,7 +484,7 @@ EncodeTiledFn encode_fn() {
 
 template <int TYPE, bool GATED, int STAGES>
 cudaError_t launch_staged(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
-                          int64_t n_out, unsigned int* err, cudaStream_t s) {
+                          int64_t n_out, unsigned int* err, cudaStream_t s, float* yf, const float* bias) {
     const size_t smem = 1024 + STAGES * (A_BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
     static bool configured_by_dev[kMaxDevices] = {};  // a function attribute is set per device
     int dev = 0;
@@ -467,25 +496,26 @@ cudaError_t launch_staged(const CUtensorMap& map, const void* w, int64_t M, int6
         configured = true;
     }
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-    qgemm_kernel<TYPE, GATED, STAGES><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err);
+    qgemm_kernel<TYPE, GATED, STAGES><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err, yf, bias);
     return cudaGetLastError();
 }
 
 template <int TYPE, bool GATED>
 cudaError_t launch_typed(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
-                         int64_t n_out, unsigned int* err, cudaStream_t s) {
+                         int64_t n_out, unsigned int* err, cudaStream_t s, float* yf, const float* bias) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    if (tiles > sms) return launch_staged<TYPE, GATED, 2>(map, w, M, N, K, y, n_out, err, s);
-    return launch_staged<TYPE, GATED, 4>(map, w, M, N, K, y, n_out, err, s);
+    if (tiles > sms) return launch_staged<TYPE, GATED, 2>(map, w, M, N, K, y, n_out, err, s, yf, bias);
+    return launch_staged<TYPE, GATED, 4>(map, w, M, N, K, y, n_out, err, s, yf, bias);
 }
 
 }  // namespace
 
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
-                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out) {
+                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out, float* yf,
+                         const float* bias) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     CUtensorMap map;
@@ -499,13 +529,33 @@ cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int6
         return cudaErrorInvalidValue;
     if (gated_n_out > 0) {
         // interleaved gate/up: N = padded rows of both; BN = 128 keeps whole pairs per CTA
-        if (type == kQ4_K) return launch_typed<kQ4_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
-        if (type == kQ6_K) return launch_typed<kQ6_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
-        return launch_typed<kQ8_0, true>(map, tiles, M, N, K, y, gated_n_out, err, s);
+        if (type == kQ4_K) return launch_typed<kQ4_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s, yf, nullptr);
+        if (type == kQ6_K) return launch_typed<kQ6_K, true>(map, tiles, M, N, K, y, gated_n_out, err, s, yf, nullptr);
+        return launch_typed<kQ8_0, true>(map, tiles, M, N, K, y, gated_n_out, err, s, yf, nullptr);
     }
-    if (type == kQ4_K) return launch_typed<kQ4_K, false>(map, tiles, M, N, K, y, N, err, s);
-    if (type == kQ6_K) return launch_typed<kQ6_K, false>(map, tiles, M, N, K, y, N, err, s);
-    return launch_typed<kQ8_0, false>(map, tiles, M, N, K, y, N, err, s);
+    if (type == kQ4_K) return launch_typed<kQ4_K, false>(map, tiles, M, N, K, y, N, err, s, yf, bias);
+    if (type == kQ6_K) return launch_typed<kQ6_K, false>(map, tiles, M, N, K, y, N, err, s, yf, bias);
+    return launch_typed<kQ8_0, false>(map, tiles, M, N, K, y, N, err, s, yf, bias);
+}
+
+// x f32 -> bf16 (round to nearest even), the prefill GEMM's activation operand.
+__global__ void cast_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ xb, int64_t n) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 4 <= n && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const float4 v = *reinterpret_cast<const float4*>(x + i);
+        *reinterpret_cast<uint2*>(xb + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+    } else {
+        for (int64_t j = i; j < i + 4 && j < n; ++j) {
+            const __nv_bfloat16 b = __float2bfloat16_rn(x[j]);
+            xb[j] = *reinterpret_cast<const uint16_t*>(&b);
+        }
+    }
+}
+
+cudaError_t launch_cast_bf16(const float* x, uint16_t* xb, int64_t n, cudaStream_t s) {
+    const int64_t threads = (n + 3) / 4;
+    cast_bf16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, xb, n);
+    return cudaGetLastError();
 }
 
 }  // namespace ocl

@@ -560,6 +560,14 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
 // The epoch lives in device memory (so CUDA-graph replays advance it); the last
 // CTA to finish bumps it, and its parity picks one of two data buffers, so a
 // rank one launch ahead never overwrites data a peer is still reading.
+// A flag slot is single-buffered: a peer that already saw this rank's flag,
+// finished its own launch and reached the next row-split launch stores
+// epoch + 2 over epoch + 1 before this rank may have polled it.  The wait
+// therefore tests "reached" (wrap-safe signed difference), never equality.
+// That peer cannot get further: its launch epoch + 1 waits for this rank's
+// epoch + 2 flag, stored only after this rank's launch epoch has finished
+// reading (the next launch starts behind griddepcontrol.wait), so the data
+// slot of parity epoch is never overwritten while it is read.
 __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -610,7 +618,7 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
     if ((int)threadIdx.x < tp.world) {
         const unsigned int* f = my_flags + (int64_t)threadIdx.x * tp.max_groups + blockIdx.x;
         const long long t0 = clock64();
-        while (ld_acquire_sys(f) != tag) {
+        while (!tp_flag_reached(ld_acquire_sys(f), tag)) {
             if (clock64() - t0 > 2000000000LL) {
                 atomicExch(&failed_s, 1);
                 break;

@@ -84,6 +84,11 @@ struct TpArgs {
     unsigned int* flags[kTpMax] = {};
     unsigned int* ctl = nullptr;  // local: [0] epoch, [1] CTAs done this launch
 };
+// A peer's flag `v` has reached launch tag `tag` (tags grow by one per
+// launch; the signed difference keeps the test right across 2^32 wrap).
+__host__ __device__ inline bool tp_flag_reached(unsigned int v, unsigned int tag) {
+    return (int)(v - tag) >= 0;
+}
 inline size_t tp_buffer_bytes(int world, int64_t max_elems, int64_t max_groups) {
     return (size_t)2 * world * max_elems * 4 + (size_t)world * max_groups * 4 + 256;
 }
@@ -124,7 +129,14 @@ cudaError_t launch_argmax(const float* logits, int64_t rows, int64_t vocab, int3
 // Prefill GEMM: y bf16 [M, N] = x bf16 [M, K] . W^T on tcgen05 (K a multiple of 256).
 // gated_n_out > 0: W is an interleaved gate/up pair with N = 2 * 16 * row tiles
 // of each, and y bf16 [M, gated_n_out] = silu(x . gate^T) * (x . up^T).
+// yf != nullptr: f32 output instead of bf16 (y unused), plus bias[n] when given
+// (non-gated): the form ocl_q_linear uses for many rows.
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
-                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out = 0);
+                         uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out = 0,
+                         float* yf = nullptr, const float* bias = nullptr);
+// Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, size a multiple of 16).
+cudaError_t launch_prefetch_l2(const void* p, uint64_t bytes, cudaStream_t s);
+// x f32 [n] -> bf16 bits, round to nearest even.
+cudaError_t launch_cast_bf16(const float* x, uint16_t* xb, int64_t n, cudaStream_t s);
 
 }  // namespace ocl

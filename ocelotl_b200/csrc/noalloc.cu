@@ -111,13 +111,23 @@ extern "C" int ocl_q_linear_noalloc(int type, const void* w, size_t n_rows, size
     }
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (s) {  // the scratch address below belongs to the current device
+        int sdev = -1;
+        e = cudaStreamGetDevice(s, &sdev);
+        if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "q_linear_noalloc: cudaStreamGetDevice: %s", cudaGetErrorString(e));
+        if (sdev != dev)
+            return fail(OCL_ERR_INVALID, "q_linear_noalloc: stream belongs to device %d but device %d is current", sdev,
+                        dev);
+    }
     unsigned char* base = slot->scratch;
     const ocl::XPlanes planes = ocl::xplanes_carve(base, (int64_t)k);
     unsigned int* counters = reinterpret_cast<unsigned int*>(base + kPlanesBytes);
     unsigned int* flags = counters + kMaxGroups;
     float* part = reinterpret_cast<float*>(base + kPlanesBytes + kCounterBytes);
-    // The array keeps the previous call's contents: counters must start at zero.
-    e = cudaMemsetAsync(counters, 0, kCounterBytes, s);
+    // The array keeps the previous call's contents: counters must start at zero
+    // (a launch that gave up a wait can leave them raised).  The error flags
+    // after them are kept until ocl_noalloc_take_device_errors reads them.
+    e = cudaMemsetAsync(counters, 0, kMaxGroups * sizeof(unsigned int), s);
     if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "q_linear_noalloc: clearing counters: %s", cudaGetErrorString(e));
     for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
         const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
@@ -128,5 +138,26 @@ extern "C" int ocl_q_linear_noalloc(int type, const void* w, size_t n_rows, size
                                  counters, flags, false, s);
         if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "q_linear_noalloc: launch: %s", cudaGetErrorString(e));
     }
+    return OCL_OK;
+}
+
+extern "C" int ocl_noalloc_take_device_errors(void* stream, unsigned int* timeouts) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "noalloc_take_device_errors: cudaGetDevice: %s", cudaGetErrorString(e));
+    DeviceSlot* slot = nullptr;
+    int rc = setup(dev, slot);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int* flags = reinterpret_cast<unsigned int*>(slot->scratch + kPlanesBytes) + kMaxGroups;
+    unsigned int h[2] = {0, 0};
+    e = cudaMemcpyAsync(h, flags, sizeof h, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, sizeof h, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "noalloc_take_device_errors: %s", cudaGetErrorString(e));
+    if (timeouts) *timeouts = h[1];
+    if (h[1] != 0)
+        return fail(OCL_ERR_TIMEOUT, "q_linear_noalloc: %u bounded device wait(s) gave up since the last check; the "
+                    "outputs of the affected calls are incomplete", h[1]);
     return OCL_OK;
 }

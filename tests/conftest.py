@@ -28,3 +28,18 @@ def backend():
     build()
     from ocelotl_b200 import CudaKernelBackend
     return CudaKernelBackend(0)
+
+
+def pytest_terminal_summary(terminalreporter):
+    import json
+    import os
+    from tests.tolerance import RECORDED
+    if not RECORDED:
+        return
+    terminalreporter.section("achieved parity errors (asserted metric first)")
+    for name in sorted(RECORDED):
+        terminalreporter.write_line(f"{name}: " + ", ".join(f"{k}={v:.3g}" for k, v in RECORDED[name].items()))
+    path = os.environ.get("OCL_PARITY_LOG")
+    if path:
+        with open(path, "w") as f:
+            json.dump(RECORDED, f, indent=1, sort_keys=True)

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.tolerance import GEMV_RTOL, normwise_err, rel_err
+from tests.tolerance import GEMV_RTOL, gemv_err, normwise_err, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -30,7 +30,7 @@ def run_case(backend, oracle, t, n, k, rows, seed=1, bias=True, threads=8):
 @pytest.mark.parametrize("rows", [1, 2, 3, 4, 5, 8, 11, 16])
 def test_gemv_small_shapes(backend, oracle, t, rows):
     got, ref = run_case(backend, oracle, t, 100, 768, rows)
-    e = rel_err(got, ref)
+    e = gemv_err(f"gemv.small.{NAMES[t]}.rows{rows}", got, ref)
     assert e <= GEMV_RTOL, (NAMES[t], rows, e, normwise_err(got, ref))
 
 
@@ -45,7 +45,7 @@ def test_gemv_more_than_16_rows_is_chunked(backend, oracle, t, rows):
 @pytest.mark.parametrize("rows", [1, 16])
 def test_gemv_baseline_shapes(backend, oracle, t, n, k, rows):
     got, ref = run_case(backend, oracle, t, n, k, rows, bias=False)
-    e = rel_err(got, ref)
+    e = gemv_err(f"gemv.baseline.{NAMES[t]}.{n}x{k}.rows{rows}", got, ref)
     assert e <= GEMV_RTOL, (NAMES[t], n, k, rows, e, normwise_err(got, ref))
 
 
@@ -129,7 +129,7 @@ def test_unsupported_before_launch(backend):
 def test_gemv_single_row_balanced_ranges(backend, oracle, t, n, k):
     """Single row: record ranges cut row tiles across warps and CTAs (ragged n, k, bias)."""
     got, ref = run_case(backend, oracle, t, n, k, 1, seed=9)
-    e = rel_err(got, ref)
+    e = gemv_err(f"gemv.ragged.{NAMES[t]}.{n}x{k}", got, ref)
     assert e <= GEMV_RTOL, (NAMES[t], n, k, e, normwise_err(got, ref))
     assert backend.take_device_errors() == (0, 0)
 
@@ -180,3 +180,4 @@ def test_unaligned_activation_rows(backend, oracle):
         backend.synchronize()
         ref = oracle.q_linear(14, blocks.numpy(), xs[:m].numpy(), m, k, n)
         assert rel_err(y.cpu().numpy(), ref) <= GEMV_RTOL
+

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.tolerance import GEMV_RTOL, normwise_err, rel_err
+from tests.tolerance import GEMV_RTOL, gated_gemv_err, gemv_err, normwise_err, record_err, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -31,9 +31,11 @@ def test_gated_gemv_matches_oracle(backend, oracle, t, rows, hidden, inter):
     act = torch.empty(rows, inter, device="cuda")
     backend.linear_gated(pair, xd, rows, act)
     backend.synchronize()
-    ref = oracle.q_gated(t, gb, ub, x, rows, hidden, inter, threads=8)
-    e = rel_err(act.cpu().numpy(), ref)
-    assert e <= 2 * GEMV_RTOL, (t, rows, e, normwise_err(act.cpu().numpy(), ref))
+    gy = oracle.q_linear(t, gb, x, rows, hidden, inter, threads=8)
+    uy = oracle.q_linear(t, ub, x, rows, hidden, inter, threads=8)
+    e = gated_gemv_err(act.cpu().numpy(), gy, uy)
+    record_err(f"gated_gemv.t{t}.rows{rows}.{hidden}x{inter}", e)
+    assert e <= GEMV_RTOL, (t, rows, e)
 
 
 @pytest.mark.parametrize("rows", [1, 8, 16])
@@ -45,8 +47,11 @@ def test_gated_gemv_llama_shape(backend, oracle, rows):
     act = torch.empty(rows, inter, device="cuda")
     backend.linear_gated(pair, torch.from_numpy(x).cuda(), rows, act)
     backend.synchronize()
-    ref = oracle.q_gated(12, gb, ub, x, rows, hidden, inter, threads=16)
-    assert rel_err(act.cpu().numpy(), ref) <= 2 * GEMV_RTOL
+    gy = oracle.q_linear(12, gb, x, rows, hidden, inter, threads=16)
+    uy = oracle.q_linear(12, ub, x, rows, hidden, inter, threads=16)
+    e = gated_gemv_err(act.cpu().numpy(), gy, uy)
+    record_err(f"gated_gemv.llama.rows{rows}", e)
+    assert e <= GEMV_RTOL, e
     assert backend.take_device_errors() == (0, 0)
 
 
@@ -81,11 +86,19 @@ def test_mlp_gated_silu_matches_oracle(backend, oracle, t, td, rows):
     backend.synchronize()
     ref_act, ref_out = oracle.q_mlp_gated_silu(t, gb, ub, td, db, x, rows, hidden, inter, threads=8)
     a = act.cpu().numpy().reshape(rows, inter)
-    assert rel_err(a, ref_act) <= 2 * GEMV_RTOL
+    gy = oracle.q_linear(t, gb, x, rows, hidden, inter, threads=8)
+    uy = oracle.q_linear(t, ub, x, rows, hidden, inter, threads=8)
+    e = gated_gemv_err(a, gy, uy)
+    record_err(f"mlp_gated_silu.act.t{t}.rows{rows}", e)
+    assert e <= GEMV_RTOL, e
     # the down projection alone, on the device's own act
     down_only = oracle.q_linear(td, db, a, rows, inter, hidden, threads=8)
-    assert rel_err(out.cpu().numpy().reshape(rows, hidden), down_only) <= GEMV_RTOL
-    assert normwise_err(out.cpu().numpy().reshape(rows, hidden), ref_out) <= 2e-3
+    assert gemv_err(f"mlp_gated_silu.down.t{t}.rows{rows}", out.cpu().numpy().reshape(rows, hidden),
+                    down_only) <= GEMV_RTOL
+    # end to end the act error carries through down: normwise it stays at the GEMV bound
+    ne = normwise_err(out.cpu().numpy().reshape(rows, hidden), ref_out)
+    record_err(f"mlp_gated_silu.out_normwise.t{t}.rows{rows}", ne)
+    assert ne <= GEMV_RTOL
 
 
 def test_mlp_doc_example_host_slices(backend):
