@@ -236,25 +236,6 @@ def graph_of(fn, be, torch):
     return g
 
 
-def chain(be, torch, calls, pf):
-    """Run calls [(weight, fn)] in order on the current stream.  With a side
-    stream `pf`, the weight of call i + 1 is prefetched into L2 (ocl_q_prefetch_l2)
-    while call i runs: the prefetch waits for call i - 1, i.e. it starts when call
-    i does.  An entry with fn None is only prefetched (the next graph's first
-    weight).  The side stream joins the current one at the end."""
-    main = torch.cuda.current_stream()
-    for i, (w, fn) in enumerate(calls):
-        if pf is not None and i + 1 < len(calls):
-            ev = torch.cuda.Event()
-            ev.record(main)
-            pf.wait_event(ev)
-            be.prefetch_l2(calls[i + 1][0], pf)
-        if fn is not None:
-            fn()
-    if pf is not None:
-        main.wait_stream(pf)
-
-
 def bf16_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -494,7 +475,7 @@ SINGLE_GEMVS = [  # (key, type, out_features, in_features)
 ]
 
 
-def run_single_gemvs(be, args, torch, synth, dev, peak, pf=None):
+def run_single_gemvs(be, args, torch, synth, dev, peak):
     """Back-to-back calls of one GEMV shape at M = 1 over distinct weight copies
     (>= 4x L2 together, so every call streams from HBM), in a CUDA graph."""
     out = {}
@@ -510,14 +491,6 @@ def run_single_gemvs(be, args, torch, synth, dev, peak, pf=None):
         gbs = b / (us * 1e-6) / 1e9
         out[key] = {"us": round(us, 3), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes": b,
                     "copies": copies}
-        if pf is not None:  # the same calls with the next copy prefetched into L2 during each call
-            calls = [(w, lambda w=w: be.linear_dev(w, x, 1, y)) for w in ws] + [(ws[0], None)]
-            g2 = graph_of(lambda: chain(be, torch, calls, pf), be, torch)
-            us2 = time_graphs([g2], max(10, args.steps // 10), torch) / copies
-            gbs2 = b / (us2 * 1e-6) / 1e9
-            out[key].update({"us_prefetch": round(us2, 3), "GB/s_prefetch": round(gbs2, 1),
-                             "frac_prefetch": round(gbs2 / peak, 4)})
-            del g2
         del g
         for w in ws:
             w.quant.free()
@@ -618,14 +591,10 @@ def run_ocelotl(args):
     ys = {name: torch.empty(m, n, device=dev, dtype=torch.float32) for name, t, n, k, _ in shards}
     xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
 
-    pf = torch.cuda.Stream(device=dev) if args.prefetch else None
-
     def step(c):
         ws = weights[c]
-        calls = [(ws[name].weight, lambda name=name: ws[name].forward(xs[xin[name]], m, ys[name]))
-                 for name, *_ in shards]
-        calls.append((weights[(c + 1) % copies][shards[0][0]].weight, None))
-        chain(be, torch, calls, pf)
+        for name, t, n, k, sp in shards:
+            ws[name].forward(xs[xin[name]], m, ys[name])
 
     # ---- device-resident timing: one graph per weight copy --------------------
     if tp > 1:
@@ -775,7 +744,7 @@ def run_ocelotl(args):
         return tmo == 0
     layer_ok = check("layer")
     peak_gbs, _ = peaks()
-    single = run_single_gemvs(be, args, torch, synth, dev, peak_gbs, pf) if (args.single and tp == 1) else None
+    single = run_single_gemvs(be, args, torch, synth, dev, peak_gbs) if (args.single and tp == 1) else None
     if single is not None and not check("single_gemvs"):
         single = None
     fused = run_fused_mlp(be, weights, xs, sh, m, copies, args, torch, dev) if (args.fused_mlp and tp == 1) \
@@ -915,8 +884,6 @@ def main():
                     help="also time the layer with gate+up as one fused gated pass (ocl_q_linear_gated)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--single", type=int, default=1, help="also time single GEMV shapes at M = 1")
-    ap.add_argument("--prefetch", type=int, default=1,
-                    help="prefetch the next projection's weight into L2 on a side stream (ocl_q_prefetch_l2)")
     ap.add_argument("--case", choices=["gemv", "gemm"], help="run a small profiling case instead of the bench")
     ap.add_argument("--case-shape", default="12:14336:4096")
     args = ap.parse_args()

@@ -217,17 +217,6 @@ OCL_API int ocl_q_linear_noalloc(int ggml_type, const void* w_tiled_dev, size_t 
  * non-zero. */
 OCL_API int ocl_noalloc_take_device_errors(void* stream, unsigned int* timeouts);
 
-/* Pull weight `w` into L2 ahead of the call that reads it, on `stream`
- * (cudaStream_t; normally a side stream, since on the stream of the GEMVs it
- * would only run between them).  A decode step is a chain of dependent GEMVs,
- * and between one call finishing and the next one streaming (activation split,
- * kernel hand-off) HBM sits idle; prefetching the NEXT projection's weight
- * while the current one runs fills that gap, and the GEMV then reads its
- * records from L2.  A hint only: no result changes, no ordering against other
- * work is needed, and a weight evicted before use is read from HBM as usual.
- * Keep at most the next one or two weights in flight (L2 is 126 MB). */
-OCL_API int ocl_q_prefetch_l2(ocl_ctx* ctx, const ocl_qbuf* w, void* stream);
-
 /* Prefill: y bf16 [rows, out_features] = x bf16 [rows, in_features] . W^T, f32
  * accumulate on tcgen05 tensor cores (weights dequantized to bf16 tiles in
  * shared memory).  Tolerance vs the f32 oracle on the same bf16-rounded x:

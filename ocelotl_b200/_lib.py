@@ -30,7 +30,6 @@ SIGNATURES = {
     "ocl_synchronize": (C.c_int, [_vp]),
     "ocl_set_pdl": (C.c_int, [_vp, C.c_int]),
     "ocl_set_gemm_min_rows": (C.c_int, [_vp, _sz]),
-    "ocl_q_prefetch_l2": (C.c_int, [_vp, _vp, _vp]),
     "ocl_backend_id": (C.c_char_p, []),
     "ocl_abi_version": (C.c_int, []),
     "ocl_q_upload": (C.c_int, [_vp, C.c_int, _vp, _sz, _sz, C.c_int, C.POINTER(_vp)]),

@@ -331,11 +331,6 @@ class CudaKernelBackend:
             self._ctx, comm.handle, w.handle, C.c_void_p(x.data_ptr()), rows, w.k, w.n_rows,
             C.c_void_p(bias.data_ptr()) if bias is not None else None, C.c_void_p(out.data_ptr())))
 
-    def prefetch_l2(self, weight, stream: torch.cuda.Stream | None = None) -> None:
-        """Hint: pull a weight into L2 on `stream` (a side stream) before the call that reads it."""
-        w = self._quant_weight(weight)
-        self._check(self._lib.ocl_q_prefetch_l2(self._ctx, w.handle, C.c_void_p(stream.cuda_stream if stream else 0)))
-
     def set_gemm_min_rows(self, rows: int) -> None:
         """Rows at which linear_d switches to the bf16 tcgen05 GEMM (2e-2 bound); 0 = never."""
         self._check(self._lib.ocl_set_gemm_min_rows(self._ctx, rows))

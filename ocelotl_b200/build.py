@@ -17,7 +17,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libocelotl_cuda.so"
 
-SOURCES = ["api.cu", "repack.cu", "gemv.cu", "noalloc.cu", "gemm.cu", "argmax.cu", "prefetch.cu"]
+SOURCES = ["api.cu", "repack.cu", "gemv.cu", "noalloc.cu", "gemm.cu", "argmax.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -780,19 +780,6 @@ int ocl_q_mlp_gated_silu(ocl_ctx* ctx, const ocl_qbuf* gate_up, const ocl_qbuf* 
     return q_linear_locked(ctx, down, act_dev, rows, nullptr, out_dev);
 }
 
-int ocl_q_prefetch_l2(ocl_ctx* ctx, const ocl_qbuf* w, void* stream) {
-    if (!ctx) return OCL_ERR_INVALID;
-    std::lock_guard<std::mutex> lk(ctx->mu);
-    if (!w) return fail(ctx, OCL_ERR_INVALID, "prefetch_l2: weight is null");
-    if (w->device != ctx->device)
-        return fail(ctx, OCL_ERR_INVALID, "weight lives on device %d but the context is on device %d", w->device,
-                    ctx->device);
-    DeviceGuard guard(ctx->device);
-    OCL_CUDA(ctx, ocl::launch_prefetch_l2(w->dev, (uint64_t)w->bytes, static_cast<cudaStream_t>(stream)),
-             "prefetch_l2 launch");
-    return OCL_OK;
-}
-
 int ocl_set_gemm_min_rows(ocl_ctx* ctx, size_t rows) {
     if (!ctx) return OCL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(ctx->mu);

@@ -134,8 +134,6 @@ cudaError_t launch_argmax(const float* logits, int64_t rows, int64_t vocab, int3
 cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int64_t K, const uint16_t* x,
                          uint16_t* y, unsigned int* err, cudaStream_t s, int64_t gated_n_out = 0,
                          float* yf = nullptr, const float* bias = nullptr);
-// Bulk L2 prefetch of [p, p + bytes) (16-byte aligned, size a multiple of 16).
-cudaError_t launch_prefetch_l2(const void* p, uint64_t bytes, cudaStream_t s);
 // x f32 [n] -> bf16 bits, round to nearest even.
 cudaError_t launch_cast_bf16(const float* x, uint16_t* xb, int64_t n, cudaStream_t s);
 
