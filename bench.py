@@ -279,58 +279,66 @@ def run_prefill(be, ws, sh, args, torch):
     return out
 
 
-def run_stack(be, args, torch, synth, dev):
-    """8B linear stack: 32 decoder layers' projections + Q6_K output head + Q8_0 embedding rows, per decode token."""
+def run_stack(be, args, torch, synth, dev, rank=0, tp=1, comm=None, group=None):
+    """8B linear stack: 32 decoder layers' projections + Q6_K output head + Q8_0 embedding rows,
+    per decode token.  Under TP (tp > 1): q/k/v and the gate/up pair split by output rows
+    (the pair stays local: act is split the same way), o and down by input columns with
+    the cross-rank sum fused into the GEMV, the head split by vocabulary rows with a
+    cross-rank greedy pick (TPHead); the embedding table is replicated (one row per token)."""
+    from ocelotl_b200.tp import TPHead, TPLinear, _range
+    import torch.distributed as dist
     n_layers, vocab = 32, 128256
+    shards = [(nm, t, n // tp, k, sp) if sp == "col" else (nm, t, n, k // tp, sp) for nm, t, n, k, sp in LAYER]
+    sh = {nm: (t, n, k, sp) for nm, t, n, k, sp in shards}
     layers = []
     for li in range(n_layers):
         ws = {}
-        for name, t, n, k, _ in LAYER:
-            blocks = synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.{name}", device=dev)
-            ws[name] = be.upload_quant(t, blocks, n, k)
-            del blocks
+        for nm in ("qkv", "o", "down"):
+            t, n, k, sp = sh[nm]
+            ws[nm] = TPLinear(be, t, synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.{nm}.r{rank}", device=dev),
+                              n, k, "out" if (sp == "col" or tp == 1) else "in", comm=comm, group=group)
         # the model path runs gate and up as one gated pass (ocelotl_b200/model.py)
-        ws["gate_up"] = be.pair_gated(ws["gate"], ws["up"])
-        ws.pop("gate").quant.free()
-        ws.pop("up").quant.free()
+        t, n, k, _ = sh["gate"]
+        g = be.upload_quant(t, synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.gate.r{rank}", device=dev), n, k)
+        u = be.upload_quant(t, synth.quant_blocks(t, n, k, args.seed, f"stack.{li}.up.r{rank}", device=dev), n, k)
+        ws["gate_up"] = be.pair_gated(g, u)
+        g.quant.free()
+        u.quant.free()
         layers.append(ws)
-    head = be.upload_quant(Q6_K, synth.quant_blocks(Q6_K, vocab, HIDDEN, args.seed, "stack.head", device=dev),
-                           vocab, HIDDEN)
+    v0, v1 = _range(vocab, rank, tp)
+    head = TPHead(be, Q6_K, synth.quant_blocks(Q6_K, v1 - v0, HIDDEN, args.seed, f"stack.head.r{rank}", device=dev),
+                  v0, v1, HIDDEN, rank, tp, group=group)
     emb = be.upload_quant(8, synth.quant_blocks(8, vocab, HIDDEN, args.seed, "stack.emb", device=dev), vocab, HIDDEN)
     torch.cuda.synchronize()
-    res = {}
+    res = {"tp": tp}
     wbytes_total = n_layers * sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER) + wbytes(Q6_K, vocab, HIDDEN)
     for m in (1, 8):
         ids = torch.randint(0, vocab, (m,), dtype=torch.int32, device=dev)
         h = torch.empty(m, HIDDEN, device=dev)
-        xs = {name: synth.activations(m, k, args.seed, f"stack.x.{name}", device=dev) for name, t, n, k, _ in LAYER}
-        ys = {name: torch.empty(m, n, device=dev) for name, t, n, k, _ in LAYER}
-        logits = torch.empty(m, vocab, device=dev)
-        next_ids = torch.empty(m, dtype=torch.int32, device=dev)
-        xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
+        xs = {nm: synth.activations(m, sh[nm][2], args.seed, f"stack.x.{nm}", device=dev) for nm in sh}
+        ys = {nm: torch.empty(m, sh[nm][1], device=dev) for nm in sh}
+        logits = torch.empty(m, v1 - v0, device=dev)
+        next_ids = torch.empty(m, dtype=torch.int64, device=dev)
+        act = torch.empty(m, sh["gate"][1], device=dev)
 
-        act = torch.empty(m, FFN, device=dev)
-
-        def token():
+        def token(m=m, ids=ids, h=h, xs=xs, ys=ys, logits=logits, next_ids=next_ids, act=act):
             be.embed_rows(emb, ids, h)
             for ws in layers:
-                be.linear_dev(ws["qkv"], xs["qkv"], m, ys["qkv"])
-                be.linear_dev(ws["o"], xs["o"], m, ys["o"])
+                ws["qkv"].forward(xs["qkv"], m, ys["qkv"])
+                ws["o"].forward(xs["o"], m, ys["o"])
                 be.linear_gated(ws["gate_up"], xs["gate"], m, act)
-                be.linear_dev(ws["down"], xs["down"], m, ys["down"])
-            be.linear_dev(head, h, m, logits)
-            be.greedy_sample(logits, out=next_ids)
-
-        def head_only():
-            be.linear_dev(head, h, m, logits)
-            be.greedy_sample(logits, out=next_ids)
-        gh = graph_of(head_only, be, torch)
-        head_us = time_graphs([gh], 20, torch)
-        del gh
+                ws["down"].forward(xs["down"], m, ys["down"])
+            head.forward(h, m, logits, next_ids)
+        token()  # communicators and scratch set up before capture
+        torch.cuda.synchronize()
+        if tp > 1:
+            dist.barrier()
         g = graph_of(token, be, torch)
         for _ in range(3):
             g.replay()
         torch.cuda.synchronize()
+        if tp > 1:
+            dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
         a.record()
@@ -339,16 +347,17 @@ def run_stack(be, args, torch, synth, dev):
         b.record()
         torch.cuda.synchronize()
         us = 1e3 * a.elapsed_time(b) / reps
+        if tp > 1:
+            t_ = torch.tensor([us])
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            us = float(t_.item())
         alg = wbytes_total + m * wbytes(8, 1, HIDDEN)
         res[str(m)] = {"token_us": round(us, 1), "tok_s": round(m / (us * 1e-6), 1),
-                       "GB/s": round(alg / (us * 1e-6) / 1e9, 1), "alg_bytes": alg,
-                       "head_argmax_us": round(head_us, 2),
-                       "head_GB/s": round(wbytes(Q6_K, vocab, HIDDEN) / (head_us * 1e-6) / 1e9, 1)}
+                       "GB/s": round(alg / (us * 1e-6) / 1e9, 1), "alg_bytes": alg}
         del g
     res["note"] = ("per decode step: Q8_0 embedding gather, 32 x (qkv, o, gated gate+up pass, down) quantized GEMVs "
-                   "and the "
-                   "Q6_K output head + greedy argmax over the 128256 logits, one CUDA graph; linear layers only (no attention "
-                   "or norms); head_argmax_us = head GEMV + argmax alone")
+                   "and the Q6_K output head + greedy argmax over the 128256 logits (vocab split over the ranks "
+                   "under TP), one CUDA graph; linear layers only (no attention or norms)")
     del layers, head, emb
     torch.cuda.synchronize()
     return res
@@ -364,43 +373,49 @@ LAYER_70B = [  # hidden 8192, GQA kv 1024 (q 8192 + k 1024 + v 1024), ffn 28672
 
 
 def run_tp70b(be, args, torch, synth, dev, rank, tp, comm, group):
-    """70B-shaped layer's projections under tensor parallelism (per decode token)."""
+    """70B-shaped decoder stack's projections under tensor parallelism, per decode token:
+    80 distinct layers (43.3 GB of weights over the TP ranks) in one CUDA graph, so every
+    token streams every layer's weights from HBM once; nothing is extrapolated."""
     from ocelotl_b200.tp import TPLinear
     import torch.distributed as dist
+    n_layers = args.layers_70b
     shards = [(nm, t, n // tp, k, sp) if sp == "col" else (nm, t, n, k // tp, sp) for nm, t, n, k, sp in LAYER_70B]
     per_gpu = sum(wbytes(t, n, k) for _, t, n, k, _ in shards)
-    copies = max(1, -(-4 * L2_BYTES // per_gpu))
     layers = []
-    for c in range(copies):
-        layers.append({nm: TPLinear(be, t, synth.quant_blocks(t, n, k, args.seed, f"70b.{nm}.r{rank}.c{c}", device=dev),
+    for li in range(n_layers):
+        layers.append({nm: TPLinear(be, t, synth.quant_blocks(t, n, k, args.seed, f"70b.{nm}.l{li}.r{rank}",
+                                                              device=dev),
                                     n, k, "out" if sp == "col" else "in", comm=comm, group=group)
                        for nm, t, n, k, sp in shards})
+    torch.cuda.synchronize()
     total = sum(wbytes(t, n, k) for _, t, n, k, _ in LAYER_70B)
-    out = {"per_gpu_weight_bytes": per_gpu, "layer_weight_bytes": total, "copies": copies}
+    peak, _ = peaks()
+    out = {"layers": n_layers, "per_gpu_weight_bytes_per_layer": per_gpu, "layer_weight_bytes": total,
+           "token_weight_bytes": n_layers * total}
     xin = {"qkv": "qkv", "o": "o", "gate": "gate", "up": "gate", "down": "down"}
     for m in (1, 16):
         xs = {nm: synth.activations(m, k, args.seed, f"70b.x.{nm}.r{rank}", device=dev) for nm, t, n, k, _ in shards}
         ys = {nm: torch.empty(m, n, device=dev) for nm, t, n, k, _ in shards}
 
-        def step(c, m=m, xs=xs, ys=ys):
-            for nm, t, n, k, sp in shards:
-                layers[c][nm].forward(xs[xin[nm]], m, ys[nm])
-        for c in range(copies):
-            step(c)
+        def token(m=m, xs=xs, ys=ys):
+            for L in layers:
+                for nm, *_ in shards:
+                    L[nm].forward(xs[xin[nm]], m, ys[nm])
+        token()  # communicators and scratch set up before capture
         torch.cuda.synchronize()
         if tp > 1:
             dist.barrier()
-        gs = [graph_of(lambda c=c: step(c), be, torch) for c in range(copies)]
-        for i in range(3):
-            gs[i % copies].replay()
+        g = graph_of(token, be, torch)
+        for _ in range(2):
+            g.replay()
         torch.cuda.synchronize()
         if tp > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 30
+        reps = 5
         a.record()
-        for i in range(reps):
-            gs[i % copies].replay()
+        for _ in range(reps):
+            g.replay()
         b.record()
         torch.cuda.synchronize()
         us = 1e3 * a.elapsed_time(b) / reps
@@ -408,10 +423,12 @@ def run_tp70b(be, args, torch, synth, dev, rank, tp, comm, group):
             t_ = torch.tensor([us])
             dist.all_reduce(t_, op=dist.ReduceOp.MAX)
             us = float(t_.item())
-        out[str(m)] = {"layer_us": round(us, 1), "GB/s": round(total / (us * 1e-6) / 1e9, 1),
-                       "tok_s_80_layers": round(m / (80 * us * 1e-6), 1),
-                       "roofline_us_per_gpu": round(per_gpu / (6538.0e9) * 1e6, 1)}
-        del gs
+        roof = n_layers * per_gpu / (peak * 1e9) * 1e6
+        out[str(m)] = {"token_us": round(us, 1), "tok_s": round(m / (us * 1e-6), 1),
+                       "layer_us": round(us / n_layers, 2),
+                       "GB/s": round(n_layers * total / (us * 1e-6) / 1e9, 1),
+                       "roofline_token_us_per_gpu": round(roof, 1), "frac": round(roof / us, 4)}
+        del g
     del layers
     torch.cuda.synchronize()
     return out
@@ -752,9 +769,10 @@ def run_ocelotl(args):
     tp70 = run_tp70b(be, args, torch, synth, dev, rank, world, comm, nccl() if world > 1 else None) \
         if args.tp70b else None
     prefill = run_prefill(be, weights[0], sh, args, torch) if (args.prefill and tp == 1) else None
-    if tp70 is not None and not check("tp_70b_layer"):
+    if tp70 is not None and not check("tp_70b_stack"):
         tp70 = {"error": "device waits timed out; figures void", "wait_timeouts": errs_seen["wait_timeouts"]}
-    stack = run_stack(be, args, torch, synth, dev) if (args.stack and tp == 1) else None
+    stack = run_stack(be, args, torch, synth, dev, rank, tp, layer_comm, nccl() if tp > 1 else None) \
+        if args.stack else None
     reps = run_replicas(be, args, torch, synth, dev, rank, world) if (world > 1 and tp > 1 and args.replicas) \
         else None
     check("rest")
@@ -800,7 +818,7 @@ def run_ocelotl(args):
         if fused:
             line["layer_fused_mlp"] = fused
         if tp70:
-            line["tp_70b_layer"] = tp70
+            line["tp_70b_stack"] = tp70
         if stack:
             line["linear_stack_8b"] = stack
         if single:
@@ -877,7 +895,8 @@ def main():
                          "per GPU (weak scaling)")
     ap.add_argument("--replicas", type=int, default=1, help="N > 1 in tp mode: also time N independent replicas")
     ap.add_argument("--nccl", action="store_true", help="TP: NCCL all-reduce instead of the fused one")
-    ap.add_argument("--tp70b", type=int, default=1, help="also time the 70B-shaped layer (TP = N)")
+    ap.add_argument("--tp70b", type=int, default=1, help="also time the 70B-shaped stack (TP = N)")
+    ap.add_argument("--layers-70b", type=int, default=80, help="layers of the 70B-shaped stack")
     ap.add_argument("--prefill", type=int, default=1, help="also time the prefill GEMM (bf16 tcgen05, M = 512 / 2048)")
     ap.add_argument("--stack", type=int, default=1, help="also time the 8B linear stack per decode token")
     ap.add_argument("--fused-mlp", type=int, default=1,

@@ -229,8 +229,8 @@ __global__ void xsplit_kernel(const float* __restrict__ x, int rows, int64_t k, 
 // Shared-memory view of the activation planes of one CTA's K range.
 struct XSmem {
     int8_t* q;   // [ncp][qstride]  plane c = 3m + s, natural k order
-    int32_t* s;  // [ncp][sstride]  per-32 (Q4_K) / per-16 (Q6_K) sums of each plane (general layout);
-                 //                 single-row layout: lo/hi byte pieces of those sums, sstride bytes per row
+    int32_t* s;  // [ncp][sstride]  per-32 (Q4_K) / per-16 (Q6_K) sums of each plane as lo (0..63) and hi
+                 //                 byte pieces, per unit lo[0..n) then hi[0..n) (sstride in ints)
     float* xs;   // [mpad][umax]    block scales 2^e
     int qstride, sstride, umax;
 };
@@ -280,20 +280,19 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* rec, int l, const XSm
             H3 += s1h * u[3];
         }
         const int ca = nt * 8 + 2 * t, cb = ca + 1;
-        const int4* sa = reinterpret_cast<const int4*>(X.s + ca * X.sstride + l * 8);
-        const int4* sb = reinterpret_cast<const int4*>(X.s + cb * X.sstride + l * 8);
-        const int4 sa0 = sa[0], sa1 = sa[1], sb0 = sb[0], sb1 = sb[1];
-        const int Sa[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
-        const int Sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
-        int M0 = 0, M1 = 0, M2 = 0, M3 = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int m0 = zext_byte(mn0[j >> 2], j & 3), m1 = zext_byte(mn1[j >> 2], j & 3);
-            M0 += m0 * Sa[j];
-            M1 += m0 * Sb[j];
-            M2 += m1 * Sa[j];
-            M3 += m1 * Sb[j];
+        // min term sum_j m_j * S_j on the tensor core: A = the mins (k = j, 8 of
+        // 16 used), B column g = plane column nt*8+g's per-32 sums as lo (0..63)
+        // and hi bytes, one MMA each: M = lo + 64 * hi, exact.
+        int ml[4], mh[4];
+        {
+            const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (nt * 8 + g) * X.sstride) + l * 16 + 4 * t;
+            const uint32_t blo = t < 2 ? *reinterpret_cast<const uint32_t*>(pr) : 0u;
+            const uint32_t bhi = t < 2 ? *reinterpret_cast<const uint32_t*>(pr + 8) : 0u;
+            const uint32_t a0 = t < 2 ? mn0[t & 1] : 0u, a1 = t < 2 ? mn1[t & 1] : 0u;
+            mma_s8_k16(ml, a0, a1, blo);
+            mma_s8_k16(mh, a0, a1, bhi);
         }
+        const int M0 = ml[0] + 64 * mh[0], M1 = ml[1] + 64 * mh[1], M2 = ml[2] + 64 * mh[2], M3 = ml[3] + 64 * mh[3];
         const float xa = X.xs[(ca / 3) * X.umax + l], xb2 = X.xs[(cb / 3) * X.umax + l];
         acc[nt][0] += xa * (d0 * (float)(16 * L0 + H0) - dm0 * (float)M0);
         acc[nt][1] += xb2 * (d0 * (float)(16 * L1 + H1) - dm0 * (float)M1);
@@ -334,27 +333,30 @@ __device__ __forceinline__ void consume_q6k(const uint8_t* rec, int l, const XSm
     for (int nt = 0; nt < NT; ++nt) {
         const int8_t* xb = X.q + (nt * 8 + g) * X.qstride + l * 256 + 4 * t;
         const int ca = nt * 8 + 2 * t, cb = ca + 1;
-        const int4* sa = reinterpret_cast<const int4*>(X.s + ca * X.sstride + l * 16);
-        const int4* sb = reinterpret_cast<const int4*>(X.s + cb * X.sstride + l * 16);
         int C[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-            const int4 A = sa[j4], B = sb[j4];
-            const int SA[4] = {A.x, A.y, A.z, A.w}, SB[4] = {B.x, B.y, B.z, B.w};
+        for (int j = 0; j < 16; ++j) {
+            uint32_t a0, a1;
+            q6_frag(j, lw[j], hw[j >> 1], a0, a1);
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
+            int r[4];
+            mma_s8_k16(r, a0, a1, b0);
+            const int scg = sext_byte(sw0[j >> 2], j & 3), sch = sext_byte(sw1[j >> 2], j & 3);
+            C[0] += scg * r[0];
+            C[1] += scg * r[1];
+            C[2] += sch * r[2];
+            C[3] += sch * r[3];
+        }
+        // offset term sum_j sc_j * S_j on the tensor core: A = the 16 int8
+        // scales, B column g = plane column nt*8+g's per-16 sums as lo / hi
+        // bytes; C -= 32 * (lo + 64 * hi), exact.
+        {
+            const int8_t* pr = reinterpret_cast<const int8_t*>(X.s + (nt * 8 + g) * X.sstride) + l * 32 + 4 * t;
+            int ol[4], oh[4];
+            mma_s8_k16(ol, sw0[t], sw1[t], *reinterpret_cast<const uint32_t*>(pr));
+            mma_s8_k16(oh, sw0[t], sw1[t], *reinterpret_cast<const uint32_t*>(pr + 16));
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = 4 * j4 + jj;
-                uint32_t a0, a1;
-                q6_frag(j, lw[j], hw[j >> 1], a0, a1);
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * j);
-                int r[4];
-                mma_s8_k16(r, a0, a1, b0);
-                const int scg = sext_byte(sw0[j >> 2], j & 3), sch = sext_byte(sw1[j >> 2], j & 3);
-                C[0] += scg * (r[0] - 32 * SA[jj]);
-                C[1] += scg * (r[1] - 32 * SB[jj]);
-                C[2] += sch * (r[2] - 32 * SA[jj]);
-                C[3] += sch * (r[3] - 32 * SB[jj]);
-            }
+            for (int i = 0; i < 4; ++i) C[i] -= 32 * (ol[i] + 64 * oh[i]);
         }
         const float xa = X.xs[(ca / 3) * X.umax + l], xb2 = X.xs[(cb / 3) * X.umax + l];
         acc[nt][0] += xa * (d0 * (float)C[0]);
@@ -532,8 +534,8 @@ struct SmemMap {
 __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows) {
     const int nc = nt * 8, mpad = nt ? (nc + 2) / 3 : 1, ncp = 3 * mpad;
     const int qstride = umax * 256 + 32;
-    // ints per sum row: 4-byte sums (general layout) or 2 bytes per sum (lo/hi pieces, single row)
-    const int sstride = sum_per(type) ? (nt ? umax * sum_per(type) : umax * sum_per(type) / 2) + 4 : 0;
+    // ints per sum row: 2 bytes per sum (its lo / hi byte pieces), + 16 bytes of slack
+    const int sstride = sum_per(type) ? umax * sum_per(type) / 2 + 4 : 0;
     SmemMap m;
     m.ring = 0;
     m.bars = kWarps * stages(type, nt) * unit_bytes(type);
@@ -730,7 +732,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     float* red = reinterpret_cast<float*>(smem + map.red);
     const XSmem X{reinterpret_cast<int8_t*>(smem + map.xq), reinterpret_cast<int32_t*>(smem + map.xsum),
                   reinterpret_cast<float*>(smem + map.xs), a.umax * 256 + 32,
-                  sum_per(TYPE) ? (NT ? a.umax * sum_per(TYPE) : a.umax * sum_per(TYPE) / 2) + 4 : 0, a.umax};
+                  sum_per(TYPE) ? a.umax * sum_per(TYPE) / 2 + 4 : 0, a.umax};
 
     auto unit_src = [&](int u, uint32_t& bytes) -> const uint8_t* {
         if (TYPE == kQ8_0) {
@@ -766,16 +768,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     pdl_trigger();
     const int NU = U1 - U0;
     if (warp == 0) {
-        const uint32_t qb = (uint32_t)NU * 256, sb = (uint32_t)(NU * sum_per(TYPE) * (NT ? 4 : 2));
+        const uint32_t qb = (uint32_t)NU * 256, sb = (uint32_t)(NU * sum_per(TYPE) * 2);
         if (lane == 0) mbar_expect_tx(xbar, NCP * (qb + sb));
         __syncwarp();
         for (int c = lane; c < NCP; c += 32) {
             bulk_g2s(X.q + c * X.qstride, a.p.xq + (int64_t)c * a.p.kx + (int64_t)U0 * 256, qb, xbar);
-            if (sum_per(TYPE) && NT) {
-                const int32_t* src = (TYPE == kQ4_K) ? a.p.s32 : a.p.s16;
-                const int64_t gstride = (int64_t)(a.p.kx / 256) * sum_per(TYPE);
-                bulk_g2s(X.s + c * X.sstride, src + (int64_t)c * gstride + (int64_t)U0 * sum_per(TYPE), sb, xbar);
-            } else if (sum_per(TYPE)) {  // single row: byte pieces of the sums
+            if (sum_per(TYPE)) {  // byte pieces of the sums
                 const int8_t* src = (TYPE == kQ4_K) ? a.p.p32 : a.p.p16;
                 const int per = 2 * sum_per(TYPE);
                 bulk_g2s(X.s + c * X.sstride, src + ((int64_t)c * (a.p.kx / 256) + U0) * per, sb, xbar);
@@ -1059,8 +1057,8 @@ cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p,
                           int type) {
     // the sums the GEMV of `type` reads: byte pieces for a single row, ints otherwise
     int sums = 15;
-    if (type == kQ4_K) sums = rows == 1 ? 8 : 2;
-    else if (type == kQ6_K) sums = rows == 1 ? 4 : 1;
+    if (type == kQ4_K) sums = 8;       // per-32 byte pieces
+    else if (type == kQ6_K) sums = 4;  // per-16 byte pieces
     else if (type == kQ8_0) sums = 0;
     const int nt = rows == 1 ? 0 : (3 * rows + 7) / 8;
     const int mpad = nt ? (nt * 8 + 2) / 3 : 1;  // activation rows whose planes the GEMV reads

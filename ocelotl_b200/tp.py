@@ -119,3 +119,66 @@ class TPLinear:
             import torch.distributed as dist
             if dist.is_initialized() and dist.get_world_size(self.group) > 1:
                 dist.all_reduce(out, group=self.group)
+
+
+def merge_argmax(vals, ids):
+    """greedy_sample over a vocab split in rank order, from each shard's own answer.
+
+    vals, ids: [world, rows] -- each rank's local greedy choice (its value and its
+    GLOBAL id), ranks in vocab order.  greedy_sample (crates/runtime/src/sampling.rs:29-52)
+    scans from index 0 and moves only on a strictly greater value, so: the largest
+    value wins, ties go to the lowest id (= the lowest rank, as shards are
+    contiguous and in order), -0.0 equals +0.0, a NaN never wins -- except a NaN
+    at global index 0, which the scan never leaves (rank 0 reports id 0 with a
+    NaN value then, as the device argmax does for a NaN at its index 0).  The
+    other shards must report their largest non-NaN value (TPHead maps a NaN at a
+    shard's first element to -inf before its local argmax).
+    """
+    import torch
+    nan0 = torch.isnan(vals[0]) & (ids[0] == 0)
+    v = torch.where(torch.isnan(vals), torch.full_like(vals, float("-inf")), vals)
+    best = torch.argmax(v, dim=0)  # first maximum: the lowest rank
+    out = ids.gather(0, best[None]).squeeze(0)
+    return torch.where(nan0, torch.zeros_like(out), out)
+
+
+class TPHead:
+    """Output head split by vocabulary rows over the ranks, with a cross-rank greedy pick.
+
+    Each rank holds head rows [v0, v1) (the logits of its vocab shard), runs the
+    quantized GEMV and the device argmax on them, and the ranks exchange one
+    (value, id) pair per row (all_gather over `group`, NCCL on the GPU path);
+    merge_argmax turns those into greedy_sample's answer over the whole vocab.
+    The reference's caller: crates/runtime/src/sampling.rs:29.
+    """
+
+    def __init__(self, backend, ggml_type: int, shard_blocks, v0: int, v1: int, k: int, rank: int, world: int,
+                 group=None):
+        self.backend = backend
+        self.v0, self.n = v0, v1 - v0
+        self.rank, self.world, self.group = rank, world, group
+        self.weight = backend.upload_quant(ggml_type, shard_blocks, self.n, k)
+
+    def forward(self, h, rows: int, logits, ids_out) -> None:
+        """h [rows, k] f32, logits [rows, n_local] scratch, ids_out [rows] int64: global greedy ids."""
+        import torch
+        import torch.distributed as dist
+        be = self.backend
+        be.linear_dev(self.weight, h, rows, logits)
+        if self.v0 > 0:
+            # greedy_sample's scan never leaves a NaN at ITS index 0; for a shard
+            # that starts past global index 0 such a NaN must not hide the
+            # shard's maximum, so it is taken as -inf here
+            first = logits[:, :1]
+            first.copy_(torch.where(torch.isnan(first), torch.full_like(first, float("-inf")), first))
+        local = be.greedy_sample(logits).long()
+        vals = logits.gather(1, local[:, None]).squeeze(1)
+        gids = local + self.v0
+        if self.world == 1:
+            ids_out.copy_(gids)
+            return
+        gv = torch.empty(self.world, rows, dtype=vals.dtype, device=vals.device)
+        gi = torch.empty(self.world, rows, dtype=gids.dtype, device=gids.device)
+        dist.all_gather_into_tensor(gv, vals, group=self.group)
+        dist.all_gather_into_tensor(gi, gids, group=self.group)
+        ids_out.copy_(merge_argmax(gv, gi))

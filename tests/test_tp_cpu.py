@@ -71,3 +71,69 @@ def test_row_split_rejects_ragged_blocks():
     from ocelotl_b200 import UnsupportedError, tp
     with pytest.raises(UnsupportedError):
         tp.shard_in(np.zeros(2 * 3 * 144, np.uint8), 12, 2, 768, 0, 2)
+
+
+def _head_worker(rank, world, port, logits, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import oracle
+    from ocelotl_b200.tp import _range, merge_argmax
+    rows, vocab = logits.shape
+    v0, v1 = _range(vocab, rank, world)
+    shard = logits[:, v0:v1].copy()
+    if v0 > 0:  # as TPHead: a NaN at a later shard's first element must not hide its maximum
+        shard[:, 0] = np.where(np.isnan(shard[:, 0]), -np.inf, shard[:, 0])
+    # each rank's local greedy answer on its shard (the oracle stands in for the device argmax)
+    local = np.array([oracle.greedy_sample(shard[r]) for r in range(rows)])
+    vals = torch.from_numpy(logits[np.arange(rows), v0 + local].astype(np.float32))
+    vals = torch.where(torch.isnan(vals) & torch.tensor(v0 > 0), torch.tensor(float("-inf")), vals)
+    gids = torch.from_numpy(local + v0)
+    gv = [torch.empty_like(vals) for _ in range(world)]
+    gi = [torch.empty_like(gids) for _ in range(world)]
+    dist.all_gather(gv, vals)
+    dist.all_gather(gi, gids)
+    got = merge_argmax(torch.stack(gv), torch.stack(gi)).numpy()
+    if rank == 0:
+        q.put(got.tolist())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_vocab_split_greedy_matches_full_scan(world):
+    """Head split by vocab over ranks: the merged pick equals greedy_sample over all logits
+    (ties across shards, -0.0 / +0.0, NaN at index 0, NaN elsewhere and at a shard's
+    first element next to the maximum, all -inf)."""
+    import oracle
+    rng = np.random.default_rng(3)
+    vocab = 1000
+    rows = [rng.standard_normal(vocab).astype(np.float32) for _ in range(6)]
+    tie = np.full(vocab, -1.0, np.float32)
+    tie[[130, 700, 999]] = 5.0           # equal maxima in different shards -> lowest id
+    rows.append(tie)
+    z = np.full(vocab, -1.0, np.float32)
+    z[600], z[10] = 0.0, -0.0            # -0.0 at a lower id ties with +0.0
+    rows.append(z)
+    n0 = rng.standard_normal(vocab).astype(np.float32)
+    n0[0] = np.nan                        # NaN at index 0: the scan stays at 0
+    rows.append(n0)
+    nm = rng.standard_normal(vocab).astype(np.float32)
+    nm[[5, 250, 501, 502, 998]] = np.nan  # NaNs elsewhere never win
+    rows.append(nm)
+    for start in (250, 500):             # a later shard starts with NaN and holds the maximum next to it
+        sh = rng.standard_normal(vocab).astype(np.float32)
+        sh[start], sh[start + 1] = np.nan, 50.0
+        rows.append(sh)
+    rows.append(np.full(vocab, -np.inf, np.float32))
+    logits = np.stack(rows)
+    expect = [oracle.greedy_sample(r) for r in logits]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_head_worker, args=(r, world, port, logits, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert q.get(timeout=10) == expect
