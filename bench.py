@@ -848,7 +848,7 @@ def run_ocelotl(args):
 def run_profile_case(args):
     """Small single-GPU cases for ncu captures (a few launches, a few hundred MB at most).
 
-    gemv: 4 copies of one weight (> L2 together), 8 single-row calls.
+    gemv: 4 copies of one weight (> L2 together), 8 calls of `rows` activation rows (default 1).
     gemm: one weight, 3 prefill GEMMs of `rows` bf16 activations.
     --case-shape "type:n:k[:rows]" picks the matrix (default the gate projection).
     """
@@ -863,11 +863,12 @@ def run_profile_case(args):
     f = [int(v) for v in args.case_shape.split(":")]
     t, n, k = f[:3]
     if args.case == "gemv":
+        rows = f[3] if len(f) > 3 else 1
         ws = [be.upload_quant(t, synth.quant_blocks(t, n, k, 1, f"w{c}", device=dev), n, k) for c in range(4)]
-        x = synth.activations(1, k, 1, "x", device=dev)
-        y = torch.empty(1, n, device=dev)
+        x = synth.activations(rows, k, 1, "x", device=dev)
+        y = torch.empty(rows, n, device=dev)
         for i in range(8):
-            be.linear_dev(ws[i % 4], x, 1, y)
+            be.linear_dev(ws[i % 4], x, rows, y)
     else:
         rows = f[3] if len(f) > 3 else 2048
         w = be.upload_quant(t, synth.quant_blocks(t, n, k, 1, "w", device=dev), n, k)
