@@ -159,30 +159,31 @@ OCL_API int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_ho
 /* ---- tensor parallelism (one process per GPU) ----------------------------- */
 /* The reference has no multi-device code (Device::Gpu{ordinal} names one GPU,
  * crates/core/src/lib.rs:437-441); these entry points are new.
- * ocl_tp_comm_create allocates this rank's receive buffer (2 x world x max_elems
- * f32 plus world x max_groups flags) and writes its 64-byte CUDA IPC handle to
- * ipc_handle_out; the caller gathers all ranks' handles (in rank order, e.g.
- * with torch.distributed all_gather) and passes them to ocl_tp_comm_open, which
- * maps the peers' buffers (NVLink / NVSwitch peer memory).  A handle equal to
- * this rank's own maps that slot back onto this rank's buffer (loopback, used
- * to exercise the bounded wait without a second process). */
+ * ocl_tp_comm_create allocates this rank's receive buffer (packet slots, 2 x
+ * world x max_elems x 8 bytes, plus 256 bytes of launch counters; max_groups is
+ * kept for ABI stability and must be non-zero, it no longer sizes anything) and
+ * writes its 64-byte CUDA IPC handle to ipc_handle_out; the caller gathers all
+ * ranks' handles (in rank order, e.g. with torch.distributed all_gather) and
+ * passes them to ocl_tp_comm_open, which maps the peers' buffers (NVLink /
+ * NVSwitch peer memory).  A handle equal to this rank's own maps that slot back
+ * onto this rank's buffer (loopback, used to exercise the bounded wait without a
+ * second process). */
 OCL_API int ocl_tp_comm_create(ocl_ctx* ctx, int rank, int world, size_t max_elems, size_t max_groups,
                                ocl_tpcomm** out, void* ipc_handle_out);
 OCL_API int ocl_tp_comm_open(ocl_ctx* ctx, ocl_tpcomm* comm, const void* ipc_handles);
 OCL_API int ocl_tp_comm_destroy(ocl_tpcomm* comm);
-/* Device address of this rank's arrival flags, u32 [world][max_groups]: slot
- * [p][g] holds the launch tag rank p last stored for row group g.  For tests of
- * the flag protocol (e.g. a peer that is already one launch ahead). */
-OCL_API unsigned int* ocl_tp_comm_flags(ocl_tpcomm* comm);
+/* Device address of this rank's packet slots, u64 [2 parities][world][max_elems]:
+ * slot [par][p][e] holds (value bits | launch tag << 32) as rank p last stored
+ * it for output element e.  For tests of the packet protocol. */
+OCL_API unsigned long long* ocl_tp_comm_packets(ocl_tpcomm* comm);
 /* Row-split quantized linear with the all-reduce fused into the GEMV: each rank
  * holds W[:, k0:k1] and x[:, k0:k1]; every rank's y receives the sum over ranks
- * (plus bias), identical bits on every rank.  Each CTA pushes its rows to every
- * peer, signals a per-row-group flag and waits (bounded, ~1 s; a timeout is
- * counted by ocl_take_device_errors and leaves y unwritten) for the peers'
- * rows.  Every rank must issue the same sequence of these calls. */
-/* Flag protocol: launch e stores tag e + 1; a waiter accepts any tag at or past
- * its own, because a peer that finished launch e may already have stored tag
- * e + 2 into the same single slot. */
+ * (plus bias), identical bits on every rank.  Each output value goes to every
+ * rank as one 8-byte packet (value, launch tag) -- no flags, no fences -- and
+ * each rank waits (bounded, ~1 s; a timeout is counted by
+ * ocl_take_device_errors and leaves y unwritten) until every rank's packet for
+ * its outputs has arrived.  Launch e stores tag e + 1; a waiter accepts any tag
+ * at or past its own.  Every rank must issue the same sequence of these calls. */
 OCL_API int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* comm, const ocl_qbuf* w, const float* x_dev,
                                    size_t rows, size_t in_features, size_t out_features, const float* bias_dev,
                                    float* y_dev);

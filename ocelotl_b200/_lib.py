@@ -44,7 +44,7 @@ SIGNATURES = {
     "ocl_tp_comm_create": (C.c_int, [_vp, C.c_int, C.c_int, _sz, _sz, C.POINTER(_vp), _vp]),
     "ocl_tp_comm_open": (C.c_int, [_vp, _vp, _vp]),
     "ocl_tp_comm_destroy": (C.c_int, [_vp]),
-    "ocl_tp_comm_flags": (_vp, [_vp]),
+    "ocl_tp_comm_packets": (_vp, [_vp]),
     "ocl_noalloc_take_device_errors": (C.c_int, [_vp, C.POINTER(C.c_uint)]),
     "ocl_q_linear_allreduce": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ocl_q_linear_host": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _vp]),

@@ -605,7 +605,7 @@ int ocl_tp_comm_create(ocl_ctx* ctx, int rank, int world, size_t max_elems, size
     c->rank = rank;
     c->max_elems = (int64_t)max_elems;
     c->max_groups = (int64_t)max_groups;
-    c->bytes = ocl::tp_buffer_bytes(world, c->max_elems, c->max_groups);
+    c->bytes = ocl::tp_buffer_bytes(world, c->max_elems);
     cudaError_t e = cudaMalloc(&c->buf, c->bytes);
     if (e == cudaSuccess) e = cudaMemset(c->buf, 0, c->bytes);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle_out), c->buf);
@@ -653,9 +653,9 @@ int ocl_tp_comm_destroy(ocl_tpcomm* c) {
     return OCL_OK;
 }
 
-unsigned int* ocl_tp_comm_flags(ocl_tpcomm* c) {
+unsigned long long* ocl_tp_comm_packets(ocl_tpcomm* c) {
     if (!c || !c->buf) return nullptr;
-    return reinterpret_cast<unsigned int*>(static_cast<char*>(c->buf) + (size_t)2 * c->world * c->max_elems * 4);
+    return reinterpret_cast<unsigned long long*>(static_cast<char*>(c->buf) + ocl::kTpCtlBytes);
 }
 
 int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const float* x_dev, size_t rows,
@@ -676,23 +676,18 @@ int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const
     tp.world = c->world;
     tp.rank = c->rank;
     tp.max_elems = c->max_elems;
-    tp.max_groups = c->max_groups;
-    for (int p = 0; p < c->world; ++p) {
-        tp.recv[p] = static_cast<float*>(c->peer[p]);
-        tp.flags[p] = reinterpret_cast<unsigned int*>(static_cast<char*>(c->peer[p]) +
-                                                      (size_t)2 * c->world * c->max_elems * 4);
-    }
-    tp.ctl = tp.flags[c->rank] + (size_t)c->world * c->max_groups;
+    for (int p = 0; p < c->world; ++p)
+        tp.pkt[p] = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->peer[p]) + ocl::kTpCtlBytes);
+    tp.ctl = static_cast<unsigned int*>(c->buf);
     for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
         const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
         ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         if (!ocl::plan_single_split(pl, w->type, m))
             return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `fused all-reduce shape` (requested `%zu x %zu`):"
                         " supported = [activation planes of the full K within shared memory]", n, k);
-        if ((int64_t)m * (int64_t)n > c->max_elems || pl.groups > c->max_groups)
-            return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: %d x %zu outputs (%lld CTAs) exceed the communicator "
-                        "capacity (%lld elements, %lld groups)", m, n, (long long)pl.groups,
-                        (long long)c->max_elems, (long long)c->max_groups);
+        if ((int64_t)m * (int64_t)n > c->max_elems)
+            return fail(ctx, OCL_ERR_INVALID, "linear_allreduce: %d x %zu outputs exceed the communicator capacity "
+                        "(%lld elements)", m, n, (long long)c->max_elems);
         OCL_CUDA(ctx, ocl::launch_xsplit(x_dev + r0 * k, m, (int64_t)k, planes, ctx->pdl, ctx->stream, w->type),
                  "x split launch");
         OCL_CUDA(ctx,

@@ -553,29 +553,29 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
 // (w / RT) of the CTA's range.
 // ---------------------------------------------------------------------------
 // Fused tensor-parallel all-reduce of this CTA's rows (called instead of the
-// plain epilogue when a.tp.world > 1, ks == 1):
-//  1. push the rows (sum of the KW slices, no bias) into slot [rank] of every
-//     rank's receive buffer (P2P stores over NVLink; own buffer included);
-//  2. CTA barrier, then release-store flag [rank][group] = epoch + 1 on every rank;
-//  3. wait (bounded, ~1 s) until every rank's flag for this group arrived here;
-//  4. sum the world slots in rank order (+ bias): every rank gets the same bits.
-// The epoch lives in device memory (so CUDA-graph replays advance it); the last
-// CTA to finish bumps it, and its parity picks one of two data buffers, so a
-// rank one launch ahead never overwrites data a peer is still reading.
-// A flag slot is single-buffered: a peer that already saw this rank's flag,
-// finished its own launch and reached the next row-split launch stores
-// epoch + 2 over epoch + 1 before this rank may have polled it.  The wait
-// therefore tests "reached" (wrap-safe signed difference), never equality.
-// That peer cannot get further: its launch epoch + 1 waits for this rank's
-// epoch + 2 flag, stored only after this rank's launch epoch has finished
-// reading (the next launch starts behind griddepcontrol.wait), so the data
-// slot of parity epoch is never overwritten while it is read.
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// plain epilogue when a.tp.world > 1, ks == 1), as packets: every output value
+// goes to every rank (self included) as ONE 8-byte store (value bits | launch
+// tag << 32) into slot [epoch parity][rank][elem] of that rank's buffer (P2P
+// stores over NVLink); each rank polls its own slots of this parity until every
+// rank's tag has arrived (bounded, ~1 s) and sums them in rank order, so every
+// rank gets the same bits.  An aligned 8-byte store is observed whole, so a
+// value and its tag travel together: no flag, no system-scope fence and no CTA
+// barrier sits on the path.  (A first version pushed the rows, then stored one
+// release flag per (rank, row group) and spun on acquire loads; at TP = 8 it cost
+// 39 / 74 us per o / down call against 11.5 / 16.8 us for the packets.)
+// The epoch lives in device memory, so CUDA-graph replays advance it; the last
+// CTA of a launch bumps it.  Tags only grow and slots are double-buffered by
+// parity, so the wait tests "reached" (tp_flag_reached), never equality, and a
+// peer cannot overwrite a slot before it is read: its next same-parity store
+// is two launches on, and its next launch waits for this rank's tags of that
+// launch, which this rank stores only after finishing this one (the next launch
+// starts behind griddepcontrol.wait).
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red, int RT, int KW, int64_t r0) {
@@ -589,6 +589,11 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
     __syncthreads();
     const unsigned int ep = ep_s, tag = ep + 1u, par = ep & 1u;
     const int64_t nrows = RT * 16;
+    const unsigned long long* mine = nullptr;
+#pragma unroll
+    for (int p = 0; p < kTpMax; ++p)
+        if (p == tp.rank) mine = tp.pkt[p];
+    mine += (int64_t)par * tp.world * tp.max_elems;
     for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
         const int m = (int)(idx / nrows), rl = (int)(idx - (int64_t)m * nrows);
         const int tile = rl >> 4, row = rl & 15;
@@ -596,53 +601,38 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
         if (o >= a.n) continue;
         float v = 0.f;
         for (int q = 0; q < KW; ++q) v += red[((q * RT + tile) * a.rows + m) * 16 + row];
+        const unsigned long long pkt = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
         const int64_t e = ((int64_t)(par * tp.world + tp.rank)) * tp.max_elems + (int64_t)m * a.n + o;
 #pragma unroll
-        for (int p = 0; p < kTpMax; ++p)  // constant indices keep the pointer table in parameter space
-            if (p < tp.world) tp.recv[p][e] = v;
+        for (int p = 0; p < kTpMax; ++p)
+            if (p < tp.world) st_volatile_u64(tp.pkt[p] + e, pkt);
     }
-    // The CTA barrier orders every thread's pushes before the flag writers'
-    // system-scope release stores (release is cumulative), so only those
-    // threads pay for the system-scope ordering.
-    __syncthreads();
-#pragma unroll
-    for (int p = 0; p < kTpMax; ++p)
-        if (p < tp.world && (int)threadIdx.x == p)
-            st_release_sys(tp.flags[p] + (int64_t)tp.rank * tp.max_groups + blockIdx.x, tag);
-    const unsigned int* my_flags = nullptr;
-    const float* my_recv = nullptr;
-#pragma unroll
-    for (int p = 0; p < kTpMax; ++p)
-        if (p == tp.rank) {
-            my_flags = tp.flags[p];
-            my_recv = tp.recv[p];
-        }
-    if ((int)threadIdx.x < tp.world) {
-        const unsigned int* f = my_flags + (int64_t)threadIdx.x * tp.max_groups + blockIdx.x;
-        const long long t0 = clock64();
-        while (!tp_flag_reached(ld_acquire_sys(f), tag)) {
-            if (clock64() - t0 > 2000000000LL) {
-                atomicExch(&failed_s, 1);
-                break;
+    bool ok = true;
+    const long long t0 = clock64();
+    for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
+        const int m = (int)(idx / nrows);
+        const int64_t o = r0 + (idx - (int64_t)m * nrows);
+        if (o >= a.n) continue;
+        float v = 0.f;
+        for (int s2 = 0; s2 < tp.world && ok; ++s2) {
+            const unsigned long long* slot = mine + (int64_t)s2 * tp.max_elems + (int64_t)m * a.n + o;
+            unsigned long long pkt = ld_volatile_u64(slot);
+            while (!tp_flag_reached((unsigned int)(pkt >> 32), tag)) {
+                if (clock64() - t0 > 2000000000LL) {
+                    ok = false;
+                    break;
+                }
+                pkt = ld_volatile_u64(slot);
             }
+            v += __uint_as_float((unsigned int)pkt);
         }
+        if (!ok) break;
+        a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
     }
+    if (!ok) atomicExch(&failed_s, 1);
     __syncthreads();
-    if (failed_s) {
-        if (threadIdx.x == 0) atomicAdd(a.err + 1, 1u);
-    } else {
-        const float* mine = my_recv + (int64_t)par * tp.world * tp.max_elems;
-        for (int idx = threadIdx.x; idx < nrows * a.rows; idx += blockDim.x) {
-            const int m = (int)(idx / nrows);
-            const int64_t o = r0 + (idx - (int64_t)m * nrows);
-            if (o >= a.n) continue;
-            float v = 0.f;
-            for (int s2 = 0; s2 < tp.world; ++s2) v += __ldcg(mine + (int64_t)s2 * tp.max_elems + (int64_t)m * a.n + o);
-            a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
-        }
-    }
+    if (failed_s && threadIdx.x == 0) atomicAdd(a.err + 1, 1u);
     // advance the epoch once every CTA of this launch is through
-    __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(tp.ctl + 1, 1u) == gridDim.x * gridDim.y - 1) {

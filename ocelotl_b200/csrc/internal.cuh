@@ -72,25 +72,24 @@ GemvPlan plan_gemv_gated(int type, int64_t n_gate, int64_t k, int rows, int sms)
 bool plan_single_split(GemvPlan& pl, int type, int rows);
 
 // Tensor-parallel all-reduce fused into the GEMV epilogue (row-split layers).
-// Every rank owns one buffer: data [2 parities][world][max_elems] f32, then
-// flags [world][max_groups] u32, then {epoch, done counter}; peers' buffers are
-// mapped into this process (CUDA IPC over NVLink), so recv[p] / flags[p] are
-// rank p's buffer as seen from here.
+// Every rank owns one buffer: {epoch, CTAs done} (256 bytes), then packet slots
+// u64 [2 parities][world][max_elems]; peers' buffers are mapped into this
+// process (CUDA IPC over NVLink), so pkt[p] is rank p's slots as seen from here.
 constexpr int kTpMax = 8;
 struct TpArgs {
     int world = 1, rank = 0;
-    int64_t max_elems = 0, max_groups = 0;
-    float* recv[kTpMax] = {};
-    unsigned int* flags[kTpMax] = {};
+    int64_t max_elems = 0;
+    unsigned long long* pkt[kTpMax] = {};
     unsigned int* ctl = nullptr;  // local: [0] epoch, [1] CTAs done this launch
 };
-// A peer's flag `v` has reached launch tag `tag` (tags grow by one per
-// launch; the signed difference keeps the test right across 2^32 wrap).
+// A packet's tag `v` has reached launch tag `tag` (tags grow by one per launch;
+// the signed difference keeps the test right across 2^32 wrap).
 __host__ __device__ inline bool tp_flag_reached(unsigned int v, unsigned int tag) {
     return (int)(v - tag) >= 0;
 }
-inline size_t tp_buffer_bytes(int world, int64_t max_elems, int64_t max_groups) {
-    return (size_t)2 * world * max_elems * 4 + (size_t)world * max_groups * 4 + 256;
+constexpr size_t kTpCtlBytes = 256;
+inline size_t tp_buffer_bytes(int world, int64_t max_elems) {
+    return kTpCtlBytes + (size_t)2 * world * max_elems * 8;
 }
 
 struct GemvArgs {

@@ -1,14 +1,14 @@
 """GPU: the GEMV with the tensor-parallel all-reduce fused in (peer memory).
 
-Protocol (ocelotl_b200/csrc/gemv.cu, tp_epilogue): launch e stores tag e + 1
-into flag[rank][group] on every rank and waits until every rank's flag has
-reached e + 1 (a peer one launch ahead may already have stored e + 2).
+Protocol (ocelotl_b200/csrc/gemv.cu, tp_epilogue): launch e sends every output
+value to every rank as one 8-byte packet (value, tag e + 1) and waits until
+every rank's packet for its outputs has reached tag e + 1.
 
 * loopback (1 GPU): a communicator whose second rank is mapped back onto the
-  first.  With rank 1's flags never raised, the bounded wait must run out,
+  first.  With rank 1's packets never sent, the bounded wait must run out,
   report a timeout (counter and OCL_ERR_TIMEOUT), write nothing and leave the
-  context usable.  With rank 1's flags already raised past the next launches'
-  tags (a peer running ahead), no launch may time out, and y must equal the
+  context usable.  With rank 1's slots already holding tags past the next
+  launches' (a peer running ahead), no launch may time out, and y must equal the
   plain GEMV's result bit for bit (rank 1's slot holds zeros).
 * 2 and 4 GPUs (each skipped below its GPU count): row-split shards on one
   process per GPU; 120 back-to-back launches alternating the o and down shapes
@@ -73,20 +73,23 @@ def test_fused_allreduce_bounded_wait_times_out(backend, oracle):
 
 
 def test_fused_allreduce_peer_already_ahead(backend):
-    """Rank 1's flags already hold tag 6: launches with tags 1..6 must pass."""
+    """Rank 1's packets already carry tag 6: launches with tags 1..6 must pass."""
     from ocelotl_b200 import synth
     for t, n, k in ((12, 4096, 4096), (14, 4096, 14336)):
         w = backend.upload_quant(t, synth.quant_blocks(t, n, k, 5, f"ahead{t}", device="cuda"), n, k)
         c = _loopback(backend, n)
-        flags = backend._lib.ocl_tp_comm_flags(c.handle)
-        assert flags
-        max_groups = 4096
-        raised = torch.full((max_groups,), 6, dtype=torch.int32, device="cuda")
-        # flag[1][*] = 6 (the peer is up to five launches ahead of launch 1)
+        # rank 1's slots of both parities already hold (0.0, tag 6): the peer is up
+        # to five launches ahead of launch 1
         torch.cuda.synchronize()
         cudart = C.CDLL("libcudart.so.12")  # already loaded by the library
         cudart.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
-        assert cudart.cudaMemcpy(flags + max_groups * 4, raised.data_ptr(), max_groups * 4, 3) == 0  # D2D
+        pk = backend._lib.ocl_tp_comm_packets(c.handle)
+        assert pk
+        max_elems = 16 * n
+        pkt = torch.full((max_elems,), 6 << 32, dtype=torch.int64, device="cuda")
+        for par in (0, 1):
+            dst = pk + ((par * 2 + 1) * max_elems) * 8
+            assert cudart.cudaMemcpy(dst, pkt.data_ptr(), max_elems * 8, 3) == 0  # D2D
         x = synth.activations(1, k, 5, "aheadx", device="cuda")
         ref = torch.empty(1, n, device="cuda")
         backend.linear_dev(w, x, 1, ref)

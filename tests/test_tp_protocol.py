@@ -1,17 +1,19 @@
-"""CPU: the fused all-reduce's flag protocol, driven by host threads.
+"""CPU: the fused all-reduce's packet protocol, driven by host threads.
 
-ocl_q_linear_allreduce (ocelotl_b200/csrc/gemv.cu, tp_epilogue) runs this state
-machine per row group g on every rank r, launch after launch:
-  1. push the group's partial rows into slot [epoch parity][r] of every rank;
-  2. store flag[r][g] = epoch + 1 on every rank;
-  3. wait (bounded) until every rank's flag[p][g] here has *reached* epoch + 1;
-  4. sum the slots of this parity in rank order; epoch += 1.
-Each rank's flag slot is single-buffered, so a peer that is a launch ahead can
-overwrite tag e + 1 with e + 2 before a slow rank polls it.  The simulation
-makes one rank fast and the others slow and checks that the "reached" test
-(tp_flag_reached in ocelotl_b200/csrc/internal.cuh) finishes every launch with
-the exact sums, while an equality test -- the protocol as first written --
-times out.  The predicate is restated here with the same 32-bit wrap.
+ocl_q_linear_allreduce (ocelotl_b200/csrc/gemv.cu, tp_epilogue) runs this per
+output element on every rank r, launch after launch (epoch e, tag e + 1,
+parity e % 2):
+  1. store packet (value, tag) into slot [parity][r][elem] of every rank;
+  2. poll this rank's own slots [parity][*][elem] until every tag has *reached*
+     tag (tp_flag_reached in ocelotl_b200/csrc/internal.cuh, restated here with
+     the same 32-bit wrap), then sum the values in rank order; epoch += 1.
+A value and its tag are one 8-byte store, so they are observed together (the
+lock below stands in for that atomicity).  The simulation makes one rank fast
+and the others slow, so the fast rank keeps storing the next launch's packets
+into the other parity while the slow ones still read: every launch must finish
+with the exact sums, with no timeout, also across the tag wrap.  A variant that
+drops the parity double buffer shows why it is needed: the fast rank then
+overwrites packets a slow rank has not read yet.
 """
 import threading
 import time
@@ -25,81 +27,73 @@ def flag_reached(v: int, tag: int) -> bool:
     return ((v - tag) & 0xFFFFFFFF) < 0x80000000
 
 
-def flag_equal(v: int, tag: int) -> bool:
-    return v == tag
-
-
-def _simulate(world, launches, groups, reached, slow_ranks, limit_s=1.0, first_epoch=0):
-    data = np.zeros((world, 2, world, groups), dtype=np.int64)  # [owner][parity][src rank][group]
-    flags = np.zeros((world, world, groups), dtype=np.uint64)   # [owner][src rank][group]
-    flags[:] = first_epoch
-    results = np.zeros((world, launches, groups), dtype=np.int64)
-    timeouts = [0] * world
+def _simulate(world, launches, n_elem, slow_ranks, parities=2, limit_s=1.0, first_epoch=0):
+    val = np.zeros((world, parities, world, n_elem), dtype=np.int64)   # [owner][parity][src][elem]
+    tags = np.full((world, parities, world, n_elem), first_epoch, dtype=np.uint64)
+    results = np.zeros((world, launches, n_elem), dtype=np.int64)
+    bad = [0] * world
     lock = threading.Lock()
 
     def rank(r):
         rng = np.random.default_rng(r)
         for i in range(launches):
             ep = (first_epoch + i) & 0xFFFFFFFF
-            tag, par = (ep + 1) & 0xFFFFFFFF, ep & 1
-            for g in range(groups):
-                v = (r + 1) * 1000 * (i + 1) + g
-                with lock:
-                    for p in range(world):
-                        data[p, par, r, g] = v
-                    for p in range(world):  # release after the data (the lock orders them)
-                        flags[p, r, g] = tag
-            for g in range(groups):
-                if r in slow_ranks:
-                    time.sleep(float(rng.uniform(0.0, 0.002)))
-                t0 = time.monotonic()
-                ok = True
-                while True:
-                    with lock:
-                        if all(reached(int(flags[r, p, g]), tag) for p in range(world)):
-                            results[r, i, g] = int(data[r, par, :, g].sum())
+            tag, par = (ep + 1) & 0xFFFFFFFF, ep % parities
+            for e in range(n_elem):
+                v = (r + 1) * 1000 * (i + 1) + e
+                for p in range(world):
+                    with lock:  # one 8-byte store: value and tag together
+                        val[p, par, r, e] = v
+                        tags[p, par, r, e] = tag
+            if r in slow_ranks:
+                time.sleep(float(rng.uniform(0.0, 0.003)))
+            t0 = time.monotonic()
+            for e in range(n_elem):
+                acc = 0
+                for s in range(world):
+                    while True:
+                        with lock:
+                            if flag_reached(int(tags[r, par, s, e]), tag):
+                                acc += int(val[r, par, s, e])
+                                break
+                        if time.monotonic() - t0 > limit_s:
+                            bad[r] += 1
                             break
-                    if time.monotonic() - t0 > limit_s:
-                        ok = False
-                        break
-                    time.sleep(0)
-                if not ok:
-                    timeouts[r] += 1
+                        time.sleep(0)
+                results[r, i, e] = acc
     ts = [threading.Thread(target=rank, args=(r,)) for r in range(world)]
     for t in ts:
         t.start()
     for t in ts:
         t.join()
-    expect = np.array([[sum((p + 1) * 1000 * (i + 1) + g for p in range(world)) for g in range(groups)]
+    expect = np.array([[sum((p + 1) * 1000 * (i + 1) + e for p in range(world)) for e in range(n_elem)]
                        for i in range(launches)])
-    return results, expect, timeouts
+    return results, expect, bad
 
 
 @pytest.mark.parametrize("world", [2, 4])
-def test_reached_wait_survives_a_rank_running_ahead(world):
-    res, expect, timeouts = _simulate(world, launches=40, groups=4, reached=flag_reached,
-                                      slow_ranks=set(range(1, world)))
-    assert timeouts == [0] * world
+def test_packets_survive_a_rank_running_ahead(world):
+    res, expect, bad = _simulate(world, launches=40, n_elem=6, slow_ranks=set(range(1, world)))
+    assert bad == [0] * world
     for r in range(world):
         assert np.array_equal(res[r], expect)
 
 
-def test_equality_wait_loses_flags_to_a_rank_running_ahead():
-    # the single-buffered flag gets overwritten with the next launch's tag
-    res, expect, timeouts = _simulate(2, launches=12, groups=4, reached=flag_equal, slow_ranks={1},
-                                      limit_s=0.2)
-    assert sum(timeouts) > 0
-
-
-def test_reached_wait_across_tag_wrap():
-    res, expect, timeouts = _simulate(2, launches=8, groups=2, reached=flag_reached, slow_ranks={1},
-                                      first_epoch=0xFFFFFFFC)
-    assert timeouts == [0, 0]
+def test_packets_across_tag_wrap():
+    res, expect, bad = _simulate(2, launches=8, n_elem=4, slow_ranks={1}, first_epoch=0xFFFFFFFC)
+    assert bad == [0, 0]
     assert np.array_equal(res[0], expect) and np.array_equal(res[1], expect)
+
+
+def test_single_buffer_lets_a_fast_rank_overwrite_unread_packets():
+    # without the parity double buffer a reader can see the NEXT launch's value
+    # (its tag has "reached" too), so the sums go wrong
+    res, expect, bad = _simulate(2, launches=40, n_elem=6, slow_ranks={1}, parities=1)
+    assert not all(np.array_equal(res[r], expect) for r in range(2))
 
 
 def test_reached_predicate_edges():
     assert flag_reached(5, 5) and flag_reached(6, 5) and not flag_reached(4, 5)
     assert flag_reached(0, 0xFFFFFFFF)          # tag wrapped past the peer's value
     assert not flag_reached(0xFFFFFFFF, 0)      # one launch behind across the wrap
-    assert not flag_reached(0, 1)               # never-signalled slot
+    assert not flag_reached(0, 1)               # a slot never written
