@@ -23,20 +23,29 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
 #include "internal.cuh"
 
 namespace ocl {
 
 namespace {
 
-constexpr int BM = 256, BN = 128, BK = 64;  // BM = two 128-row MMA tiles sharing B
+constexpr int BN = 128, BK = 64;
+// A CTA's token tile is ACC x 128 rows (ACC = 2 or 4 TMEM accumulators of 128 x
+// 128 f32 sharing every dequantized weight tile).  ACC = 4 uses all 512 TMEM
+// columns and halves the dequantization per FLOP; x then arrives in two
+// 256-row TMA boxes per stage (a box dimension is at most 256).
 // Two shapes of the same kernel: 4 pipeline stages and one CTA per SM, or 2
 // stages and two CTAs per SM (<= 96 registers a thread, 2 x 256 TMEM columns),
 // which overlaps one CTA's epilogue and pipeline fill with the other's main
 // loop.  Measured on B200: the two-CTA form is 3-22% faster once the tile
 // grid exceeds one wave of SMs and 7-21% slower below that.
-constexpr int MMA_M = 128, ACCS = BM / MMA_M;                  // accumulators in TMEM (BN columns each)
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;  // 32 KB + 16 KB per stage
+constexpr int MMA_M = 128, BOX_M = 256;        // rows per MMA, rows per x TMA box
+constexpr int B_BYTES = BN * BK * 2;           // 16 KB per stage
+template <int ACC> struct ATile {
+    static constexpr int BM = ACC * MMA_M, BYTES = BM * BK * 2;  // 32 or 64 KB per stage
+};
 constexpr int PRODUCER_WARPS = 8, TMA_WARP = 8, MMA_WARP = 9, THREADS = 320;
 constexpr long long kWaitCycles = 2000000000LL;
 
@@ -264,11 +273,12 @@ __device__ __forceinline__ void dequant_quarter(const UnitRegs& R, int qt, int r
 // 2t+1 = up tile t; N = their total padded rows) and y [M, n_out] =
 // silu(gate) * up: each 32-column accumulator slice a thread reads is one
 // (gate, up) pair of 16-row tiles.
-template <int TYPE, bool GATED, int STAGES>
-__global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
+template <int TYPE, bool GATED, int STAGES, int ACCS>
+__global__ void __launch_bounds__(THREADS, (STAGES == 2 && ACCS == 2) ? 2 : 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, int64_t M, int64_t N,
                  int64_t K, uint16_t* __restrict__ y, int64_t n_out, unsigned int* __restrict__ err,
                  float* __restrict__ yf, const float* __restrict__ bias) {
+    constexpr int BM = ATile<ACCS>::BM, A_BYTES = ATile<ACCS>::BYTES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -341,7 +351,10 @@ __global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
                     break;
                 }
                 mb_expect_tx(&full_a[s], A_BYTES);
-                tma_load_2d(atiles + s * A_BYTES, &xmap, kb * BK, (int)m0, &full_a[s]);
+#pragma unroll
+                for (int h = 0; h < BM / BOX_M; ++h)
+                    tma_load_2d(atiles + s * A_BYTES + h * (BOX_M * BK * 2), &xmap, kb * BK, (int)m0 + h * BOX_M,
+                                &full_a[s]);
                 ++issued;
             }
             // make sure no copy is still landing when the CTA leaves
@@ -466,6 +479,12 @@ __global__ void __launch_bounds__(THREADS, STAGES == 2 ? 2 : 1)
     }
 }
 
+// 512-token tiles from 2048 tokens on (measured, 8B layer: +4.6% at M = 2048,
+// -17% at M = 512, where the tile grid no longer fills the SMs).  The gain is
+// small because one such CTA fills an SM: it halves the dequantization per
+// FLOP but also the producer warps per SM, which the two-CTA 256-token form has.
+inline bool wide_tokens(int64_t M, int64_t, int) { return M >= 2048; }
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -482,21 +501,22 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int TYPE, bool GATED, int STAGES>
+template <int TYPE, bool GATED, int STAGES, int ACCS>
 cudaError_t launch_staged(const CUtensorMap& map, const void* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
                           int64_t n_out, unsigned int* err, cudaStream_t s, float* yf, const float* bias) {
-    const size_t smem = 1024 + STAGES * (A_BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
+    const size_t smem = 1024 + STAGES * (ATile<ACCS>::BYTES + B_BYTES) + (3 * STAGES + 2) * 8;
     static bool configured_by_dev[kMaxDevices] = {};  // a function attribute is set per device
     int dev = 0;
     cudaGetDevice(&dev);
     bool& configured = configured_by_dev[dev < kMaxDevices ? dev : 0];
     if (!configured || dev >= kMaxDevices) {
-        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TYPE, GATED, STAGES, ACCS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    constexpr int BM = ATile<ACCS>::BM;
     const dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-    qgemm_kernel<TYPE, GATED, STAGES><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err, yf, bias);
+    qgemm_kernel<TYPE, GATED, STAGES, ACCS><<<grid, THREADS, smem, s>>>(map, (const uint8_t*)w, M, N, K, y, n_out, err, yf, bias);
     return cudaGetLastError();
 }
 
@@ -506,9 +526,12 @@ cudaError_t launch_typed(const CUtensorMap& map, const void* w, int64_t M, int64
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    if (tiles > sms) return launch_staged<TYPE, GATED, 2>(map, w, M, N, K, y, n_out, err, s, yf, bias);
-    return launch_staged<TYPE, GATED, 4>(map, w, M, N, K, y, n_out, err, s, yf, bias);
+    const int64_t tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
+    static const int force_acc = [] { const char* f = getenv("OCL_GEMM_ACC"); return f ? atoi(f) : 0; }();
+    const bool wide = force_acc ? force_acc == 4 : wide_tokens(M, N, sms);
+    if (wide) return launch_staged<TYPE, GATED, 2, 4>(map, w, M, N, K, y, n_out, err, s, yf, bias);
+    if (tiles > sms) return launch_staged<TYPE, GATED, 2, 2>(map, w, M, N, K, y, n_out, err, s, yf, bias);
+    return launch_staged<TYPE, GATED, 4, 2>(map, w, M, N, K, y, n_out, err, s, yf, bias);
 }
 
 }  // namespace
@@ -521,7 +544,7 @@ cudaError_t launch_qgemm(int type, const void* tiles, int64_t M, int64_t N, int6
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {BK, BM};  // one 64 x 256 bf16 box = both 128-row halves
+    const cuuint32_t box[2] = {BK, BOX_M};  // 64 x 256 bf16 per box: two 128-row MMA halves
     const cuuint32_t estr[2] = {1, 1};
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
