@@ -146,9 +146,9 @@ OCL_API int ocl_q_linear(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_dev, si
 
 /* Same with host buffers (x, bias, y in host memory), on the context stream,
  * synchronising before it returns.  The slice-based linear_out_by_in.
- * Returns OCL_ERR_TIMEOUT (KernelError) when a bounded device wait gave up
- * during the call, or in an earlier device-pointer call of this context that
- * ocl_take_device_errors has not reported yet; the counter is then cleared.
+ * Returns OCL_ERR_TIMEOUT (KernelError) when a bounded device wait of this call
+ * gave up (the context's timeout counter is then cleared; waits of earlier
+ * device-pointer calls are reported by ocl_take_device_errors).
  * Page-locked (pinned) buffers are read and written by the kernels in place
  * through unified addressing; pageable ones are copied through a device staging
  * area kept by the context.  (Environment OCL_HOST_ZEROCOPY=0 forces staging.) */

@@ -274,9 +274,12 @@ class CudaKernelBackend:
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         self._validate(x.size, rows, in_features, w.len_f32(), out_features, None if b is None else b.size,
                        out.size)
-        self._check(self._lib.ocl_q_linear_host(
-            self._ctx, w.handle, x.ctypes.data_as(C.c_void_p), rows, in_features, out_features,
-            b.ctypes.data_as(C.c_void_p) if b is not None else None, out.ctypes.data_as(C.c_void_p)))
+        # raw addresses: the argtypes are void*, and ndarray.ctypes.data_as costs microseconds a call
+        rc = self._lib.ocl_q_linear_host(
+            self._ctx, w.handle, x.__array_interface__["data"][0], rows, in_features, out_features,
+            b.__array_interface__["data"][0] if b is not None else None, out.__array_interface__["data"][0])
+        if rc:
+            self._check(rc)
 
     def gemm_bf16(self, x: torch.Tensor, weight, out: torch.Tensor | None = None) -> torch.Tensor:
         """Prefill: bf16 [rows, in] . W^T -> bf16 [rows, out] on tcgen05 tensor cores."""

@@ -32,7 +32,9 @@ struct ocl_ctx {
     size_t counter_count = 0;
     bool pdl = true;  // launch with programmatic dependent launch
     unsigned int* dev_flags = nullptr;  // [0] bad embedding ids, [1] bounded waits that gave up
-    unsigned int* host_flags = nullptr;  // pinned: the host-slice call's copy of dev_flags[1]
+    unsigned int* host_flags = nullptr;      // pinned, mapped: [0] set by a GEMV of a host-slice call whose wait gave up,
+                                             // [1] the GEMM route's copy of dev_flags[1]
+    unsigned int* host_flags_dev = nullptr;  // the device address of host_flags
     uint16_t* xbf = nullptr;  // bf16 copy of x for the prefill GEMM form, grown on demand
     size_t xbf_bytes = 0;
     size_t gemm_min_rows = 64;  // rows at which ocl_q_linear switches to the tcgen05 GEMM (0 = never)
@@ -242,8 +244,10 @@ int q_gemm_f32_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t ro
     return OCL_OK;
 }
 
-// y = x . W^T (+bias) for device pointers, any rows (16-row groups).
-int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, const float* bias, float* y) {
+// y = x . W^T (+bias) for device pointers, any rows (16-row groups).  host_err:
+// mapped host word the GEMVs set when a bounded wait gives up (host-slice calls).
+int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows, const float* bias, float* y,
+                    unsigned int* host_err = nullptr) {
     const size_t k = w->k, n = w->n_rows;
     if (use_gemm(ctx, w, rows)) return q_gemm_f32_locked(ctx, w, x, rows, bias, y, false);
     int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
@@ -258,7 +262,7 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
                  "x split launch");
         OCL_CUDA(ctx,
                  ocl::launch_gemv(w->type, w->dev, (int64_t)n, (int64_t)k, planes, m, bias, y + r0 * n, pl, ctx->part,
-                                  ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream),
+                                  ctx->counters, ctx->dev_flags, ctx->pdl, ctx->stream, nullptr, host_err),
                  "gemv launch");
     }
     return OCL_OK;
@@ -304,14 +308,15 @@ int check_gated_shapes(ocl_ctx* ctx, const ocl_qbuf* gu, size_t rows, size_t hid
     return OCL_OK;
 }
 
-// A kernel of this call (or an earlier device-pointer call not yet checked)
-// gave up a bounded wait: clear the counter and report it as KernelError.
+// A kernel of this call gave up a bounded wait: clear the device counter and
+// report it as KernelError.
 int take_timeouts(ocl_ctx* ctx, const char* op) {
-    const unsigned int n = ctx->host_flags[0];
-    ctx->host_flags[0] = 0;
-    cudaError_t e = cudaMemsetAsync(ctx->dev_flags + 1, 0, 4, ctx->stream);
+    unsigned int n = 0;
+    cudaError_t e = cudaMemcpyAsync(&n, ctx->dev_flags + 1, 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->dev_flags + 1, 0, 4, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "clear timeout counter");
+    ctx->host_flags[0] = ctx->host_flags[1] = 0;
     return fail(ctx, OCL_ERR_TIMEOUT,
                 "%s: %u bounded device wait(s) gave up (~1 s each); the output of the affected row groups is "
                 "incomplete", op, n);
@@ -350,7 +355,8 @@ int ocl_cuda_init(int device, ocl_ctx** out) {
     ctx->sms = prop.multiProcessorCount;
     e = cudaMalloc(&ctx->dev_flags, 64);
     if (e == cudaSuccess) e = cudaMemset(ctx->dev_flags, 0, 64);
-    if (e == cudaSuccess) e = cudaHostAlloc((void**)&ctx->host_flags, 64, cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&ctx->host_flags, 64, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer((void**)&ctx->host_flags_dev, ctx->host_flags, 0);
     if (e != cudaSuccess) {
         if (ctx->dev_flags) cudaFree(ctx->dev_flags);
         delete ctx;
@@ -541,17 +547,23 @@ int ocl_q_linear_host(ocl_ctx* ctx, const ocl_qbuf* w, const float* x_host, size
     }
     const bool y_mapped = yd != nullptr;
     if (!y_mapped) yd = y_stage;
+    // A GEMV whose bounded wait gives up sets host_flags[0] with a plain store
+    // to this mapped word, read after the synchronisation below (a 4-byte copy
+    // of the device counter instead cost ~9 us a call).  The GEMM route (many
+    // rows) copies the device counter into host_flags[1] instead.
+    volatile unsigned int* hf = ctx->host_flags;
+    hf[0] = hf[1] = 0;
+    const bool gemm_route = use_gemm(ctx, w, rows);
     if (e == cudaSuccess) {
-        rc = q_linear_locked(ctx, w, xd, rows, bd, yd);
+        rc = q_linear_locked(ctx, w, xd, rows, bd, yd, ctx->host_flags_dev);
         if (rc == OCL_OK && !y_mapped) e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, ctx->stream);
-        // the bounded-wait counter rides along with the result (one synchronisation)
-        if (rc == OCL_OK && e == cudaSuccess)
-            e = cudaMemcpyAsync(ctx->host_flags, ctx->dev_flags + 1, 4, cudaMemcpyDeviceToHost, ctx->stream);
+        if (rc == OCL_OK && e == cudaSuccess && gemm_route)
+            e = cudaMemcpyAsync(ctx->host_flags + 1, ctx->dev_flags + 1, 4, cudaMemcpyDeviceToHost, ctx->stream);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(ctx, e, "linear_out_by_in host path");
-    if (ctx->host_flags[0] != 0) return take_timeouts(ctx, "linear_out_by_in");
+    if (hf[0] != 0 || hf[1] != 0) return take_timeouts(ctx, "linear_out_by_in");
     return OCL_OK;
 }
 

@@ -631,7 +631,10 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
     }
     if (!ok) atomicExch(&failed_s, 1);
     __syncthreads();
-    if (failed_s && threadIdx.x == 0) atomicAdd(a.err + 1, 1u);
+    if (failed_s && threadIdx.x == 0) {
+        atomicAdd(a.err + 1, 1u);
+        if (a.host_err) *reinterpret_cast<volatile unsigned int*>(a.host_err) = 1u;
+    }
     // advance the epoch once every CTA of this launch is through
     if (threadIdx.x == 0) {
         __threadfence();
@@ -816,7 +819,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
         if (!ok) {
             // drain this warp's copies still in flight before its shared memory goes away
             for (int i = done; i < issued; ++i) mbar_wait_bounded(&bars[i % S], (uint32_t)((i / S) & 1));
-            if (lane == 0) atomicAdd(a.err + 1, 1u);
+            if (lane == 0) {
+                atomicAdd(a.err + 1, 1u);
+                if (a.host_err) *reinterpret_cast<volatile unsigned int*>(a.host_err) = 1u;
+            }
         }
     }
 
@@ -1066,8 +1072,9 @@ cudaError_t launch_xsplit(const float* x, int rows, int64_t k, const XPlanes& p,
 
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
-                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp) {
+                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp, unsigned int* host_err) {
     GemvArgs a{};
+    a.host_err = host_err;
     if (tp) {
         if (pl.ks != 1) return cudaErrorInvalidValue;
         a.tp = *tp;

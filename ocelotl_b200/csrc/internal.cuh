@@ -105,6 +105,7 @@ struct GemvArgs {
     unsigned int* err;       // [0] bad embedding ids, [1] bounded waits that gave up
     TpArgs tp;               // world > 1: sum the rows over ranks in the epilogue (ks must be 1)
     int gated;               // 1: interleaved gate/up tiles, y = silu(gate) * up over n = n_gate outputs
+    unsigned int* host_err;  // non-null: a mapped pinned host word set to 1 when a wait gives up
 };
 
 // y [rows<=16, n] = planes . W^T (+ bias), geometry from plan_gemv.  `pdl`
@@ -112,7 +113,8 @@ struct GemvArgs {
 // predecessor before reading the planes).
 cudaError_t launch_gemv(int type, const void* tiles, int64_t n, int64_t k, const XPlanes& p, int rows,
                         const float* bias, float* y, const GemvPlan& pl, float* part, unsigned int* counters,
-                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp = nullptr);
+                        unsigned int* err, bool pdl, cudaStream_t s, const TpArgs* tp = nullptr,
+                        unsigned int* host_err = nullptr);
 // act [rows<=16, n_gate] = silu(planes . Wg^T) * (planes . Wu^T) over an
 // interleaved gate/up weight, geometry from plan_gemv_gated.
 cudaError_t launch_gemv_gated(int type, const void* tiles, int64_t n_gate, int64_t k, const XPlanes& p, int rows,
