@@ -127,9 +127,9 @@ OCL_API int ocl_q_download_gguf(ocl_ctx* ctx, const ocl_qbuf* w, void* host_bloc
  * k == in_features.  Replaces KernelBackend::linear_d for a quantized weight
  * (crates/kernels/src/lib.rs:193-217) and, via ocl_q_linear_host, the slice form
  * linear_out_by_in (crates/kernels/src/lib.rs:107-116, 1939-1967).
- * rows 1..16 run the dequant-GEMV (HBM-bound); rows below the context's GEMM
- * threshold (64 by default, ocl_set_gemm_min_rows) are processed in 16-row
- * groups by the same kernel.  GEMV accuracy: the products of the integer quants
+ * rows 1..8 run the dequant-GEMV as one launch (HBM-bound); more rows below the
+ * context's GEMM threshold (64 by default, ocl_set_gemm_min_rows) are processed
+ * in 8-row groups by the same kernel (measured faster than 16-row launches).  GEMV accuracy: the products of the integer quants
  * with x are computed exactly (x split into three int8 planes per 256-k block,
  * i.e. ~21 significant bits), scaled and accumulated in f32; max relative error
  * vs the f32 CPU oracle <= 1e-3.
@@ -205,8 +205,9 @@ OCL_API int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* comm, const ocl_qbu
  * stream capture.  All calls share the array, so calls that overlap on the GPU
  * (different streams or devices' contexts racing on one device) race on it:
  * serialise them on one stream.  `stream` must belong to the current device
- * (OCL_ERR_INVALID otherwise).  Results are bit-identical to ocl_q_linear's
- * for rows <= 16 per launch (same kernels, same plan).  Errors:
+ * (OCL_ERR_INVALID otherwise).  Below ocl_q_linear's GEMM threshold the
+ * results are bit-identical to its (same kernels, same 8-row groups, same
+ * plans); this entry point never switches to the prefill GEMM.  Errors:
  * ocl_last_error(NULL).  A bounded device wait that gives up is counted in the
  * same array; read it with ocl_noalloc_take_device_errors. */
 OCL_API int ocl_q_linear_noalloc(int ggml_type, const void* w_tiled_dev, size_t n_rows, size_t k,

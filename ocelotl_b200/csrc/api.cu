@@ -253,8 +253,9 @@ int q_linear_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows
     int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
     if (rc) return rc;
     const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
-    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
-        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+    const size_t G = ocl::kGemvGroupRows;
+    for (size_t r0 = 0; r0 < rows; r0 += G) {
+        const int m = (int)((rows - r0) < G ? (rows - r0) : G);
         const ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
@@ -275,8 +276,9 @@ int q_gated_locked(ocl_ctx* ctx, const ocl_qbuf* w, const float* x, size_t rows,
     int rc = ensure_scratch(ctx, ocl::xplanes_bytes((int64_t)k));
     if (rc) return rc;
     const ocl::XPlanes planes = ocl::xplanes_carve(ctx->scratch, (int64_t)k);
-    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
-        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+    const size_t G = ocl::kGemvGroupRows;
+    for (size_t r0 = 0; r0 < rows; r0 += G) {
+        const int m = (int)((rows - r0) < G ? (rows - r0) : G);
         const ocl::GemvPlan pl = ocl::plan_gemv_gated(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         rc = ensure_split_buffers(ctx, pl);
         if (rc) return rc;
@@ -691,8 +693,8 @@ int ocl_q_linear_allreduce(ocl_ctx* ctx, ocl_tpcomm* c, const ocl_qbuf* w, const
     for (int p = 0; p < c->world; ++p)
         tp.pkt[p] = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->peer[p]) + ocl::kTpCtlBytes);
     tp.ctl = static_cast<unsigned int*>(c->buf);
-    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
-        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kGemvGroupRows) {
+        const int m = (int)((rows - r0) < (size_t)ocl::kGemvGroupRows ? (rows - r0) : ocl::kGemvGroupRows);
         ocl::GemvPlan pl = ocl::plan_gemv(w->type, (int64_t)n, (int64_t)k, m, ctx->sms);
         if (!ocl::plan_single_split(pl, w->type, m))
             return fail(ctx, OCL_ERR_UNSUPPORTED, "unsupported feature `fused all-reduce shape` (requested `%zu x %zu`):"

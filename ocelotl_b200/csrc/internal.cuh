@@ -26,6 +26,12 @@ struct XPlanes {
 constexpr int kMaxDevices = 64;  // per-device host-side caches
 constexpr int kRowsMax = 16;            // activation rows per GEMV launch
 constexpr int kColsMax = 3 * kRowsMax;  // int8 planes per launch
+// Rows per GEMV launch when a call has more: 8.  Measured (8B layer, same box):
+// 16 rows as one launch 208 us, as two 8-row launches 185 us (12 rows: 183 vs
+// 166; 9: 144 vs 140); the 16-row form's staged planes allow one CTA per SM
+// and its instruction count grows with the plane columns, so streaming the
+// weights twice costs less.  6-row groups lost (253 us at 16 rows).
+constexpr int kGemvGroupRows = 8;
 
 // Bytes of scratch the x planes need for a given K.
 constexpr size_t xplanes_bytes(int64_t k) {

@@ -101,8 +101,8 @@ extern "C" int ocl_q_linear_noalloc(int type, const void* w, size_t n_rows, size
     if (rc) return rc;
 
     // Check every 16-row group's geometry before launching anything.
-    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
-        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kGemvGroupRows) {  // the same row groups as ocl_q_linear
+        const int m = (int)((rows - r0) < (size_t)ocl::kGemvGroupRows ? (rows - r0) : ocl::kGemvGroupRows);
         const ocl::GemvPlan pl = ocl::plan_gemv(type, (int64_t)n_rows, (int64_t)k, m, slot->sms);
         if (pl.part_floats * sizeof(float) > kPartBytes || (pl.ks > 1 && (size_t)pl.groups > kMaxGroups))
             return fail(OCL_ERR_UNSUPPORTED, "unsupported feature `q_linear_noalloc shape` (requested `%zu x %zu, "
@@ -129,8 +129,8 @@ extern "C" int ocl_q_linear_noalloc(int type, const void* w, size_t n_rows, size
     // after them are kept until ocl_noalloc_take_device_errors reads them.
     e = cudaMemsetAsync(counters, 0, kMaxGroups * sizeof(unsigned int), s);
     if (e != cudaSuccess) return fail(OCL_ERR_CUDA, "q_linear_noalloc: clearing counters: %s", cudaGetErrorString(e));
-    for (size_t r0 = 0; r0 < rows; r0 += ocl::kRowsMax) {
-        const int m = (int)((rows - r0) < (size_t)ocl::kRowsMax ? (rows - r0) : ocl::kRowsMax);
+    for (size_t r0 = 0; r0 < rows; r0 += ocl::kGemvGroupRows) {  // the same row groups as ocl_q_linear
+        const int m = (int)((rows - r0) < (size_t)ocl::kGemvGroupRows ? (rows - r0) : ocl::kGemvGroupRows);
         const ocl::GemvPlan pl = ocl::plan_gemv(type, (int64_t)n_rows, (int64_t)k, m, slot->sms);
         e = ocl::launch_xsplit(x + r0 * k, m, (int64_t)k, planes, false, s, type);
         if (e == cudaSuccess)
