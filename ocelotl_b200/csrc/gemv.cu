@@ -613,19 +613,32 @@ __device__ __forceinline__ void tp_epilogue(const GemvArgs& a, const float* red,
         const int m = (int)(idx / nrows);
         const int64_t o = r0 + (idx - (int64_t)m * nrows);
         if (o >= a.n) continue;
-        float v = 0.f;
-        for (int s2 = 0; s2 < tp.world && ok; ++s2) {
-            const unsigned long long* slot = mine + (int64_t)s2 * tp.max_elems + (int64_t)m * a.n + o;
-            unsigned long long pkt = ld_volatile_u64(slot);
-            while (!tp_flag_reached((unsigned int)(pkt >> 32), tag)) {
-                if (clock64() - t0 > 2000000000LL) {
-                    ok = false;
-                    break;
+        // all ranks' slots are loaded at once and only the missing ones
+        // re-polled: one L2 round trip when everything has arrived, instead of
+        // one per rank in sequence
+        const unsigned long long* slot = mine + (int64_t)m * a.n + o;
+        unsigned long long pkt[kTpMax];
+#pragma unroll
+        for (int s2 = 0; s2 < kTpMax; ++s2)
+            pkt[s2] = s2 < tp.world ? ld_volatile_u64(slot + (int64_t)s2 * tp.max_elems) : ((unsigned long long)tag << 32);
+        for (;;) {
+            bool all = true;
+#pragma unroll
+            for (int s2 = 0; s2 < kTpMax; ++s2)
+                if (!tp_flag_reached((unsigned int)(pkt[s2] >> 32), tag)) {
+                    all = false;
+                    pkt[s2] = ld_volatile_u64(slot + (int64_t)s2 * tp.max_elems);
                 }
-                pkt = ld_volatile_u64(slot);
+            if (all) break;
+            if (clock64() - t0 > 2000000000LL) {
+                ok = false;
+                break;
             }
-            v += __uint_as_float((unsigned int)pkt);
         }
+        float v = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kTpMax; ++s2)  // rank order: identical bits on every rank
+            if (s2 < tp.world) v += __uint_as_float((unsigned int)pkt[s2]);
         if (!ok) break;
         a.y[(int64_t)m * a.n + o] = a.bias ? v + a.bias[o] : v;
     }
