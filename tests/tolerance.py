@@ -60,7 +60,7 @@ def gated_rel_err(y, g, u):
 # Every parity test records what it achieved, so the margin under each bound is
 # visible: pytest prints the table at the end of the run (tests/conftest.py),
 # and OCL_PARITY_LOG=<path> also writes it as JSON.
-SURVEY_FLOOR = 1e-3  # the stricter floor max(|r|, 1e-3 rms(r)), reported beside FLOOR
+STRICT_FLOOR = 1e-3  # the stricter floor max(|r|, 1e-3 rms(r)), reported beside FLOOR
 RECORDED: dict = {}
 
 
@@ -71,14 +71,14 @@ def record_err(name, value, **extra):
 def gemv_err(name, y, r):
     """rel_err with FLOOR (the asserted one), recorded with the 1e-3-floor and normwise figures."""
     e = rel_err(y, r)
-    record_err(name, e, err_floor_1e3=rel_err(y, r, floor=SURVEY_FLOOR), normwise=normwise_err(y, r))
+    record_err(name, e, err_floor_1e3=rel_err(y, r, floor=STRICT_FLOOR), normwise=normwise_err(y, r))
     return e
 
 
 def gemm_err(name, y, r):
     """rel_err with GEMM_FLOOR (the asserted one), recorded with the normwise figure."""
     e = rel_err(y, r, floor=GEMM_FLOOR)
-    record_err(name, e, err_floor_1e3=rel_err(y, r, floor=SURVEY_FLOOR), normwise=normwise_err(y, r))
+    record_err(name, e, err_floor_1e3=rel_err(y, r, floor=STRICT_FLOOR), normwise=normwise_err(y, r))
     return e
 
 
