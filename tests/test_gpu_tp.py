@@ -170,6 +170,25 @@ def _rank(rank, world, port, q):
     results["rows5"] = {"same": all(g == gathered[0] for g in gathered), "errs": be.take_device_errors()}
     if rank == 0:
         results["err_rows5"] = rel_err(yh, oracle.q_linear(t, blocks, x, rows, k, n, threads=8))
+    # 3) vocab-split head with the cross-rank greedy pick (TPHead): the merged ids
+    # must be greedy_sample over the gathered logits, which must match the oracle
+    vocab, hk, hrows = 5000, 512, 3
+    hblocks = synth.quant_blocks(14, vocab, hk, 9, "tphead").numpy()
+    h = synth.activations(hrows, hk, 9, "tpheadx").numpy()
+    v0, v1 = tp._range(vocab, rank, world)
+    row_bytes = (hk // 256) * 210
+    head = tp.TPHead(be, 14, np.ascontiguousarray(hblocks.reshape(vocab, row_bytes)[v0:v1]).reshape(-1), v0, v1, hk,
+                     rank, world, group=dist.new_group(backend="nccl"))
+    logits = torch.empty(hrows, v1 - v0, device="cuda")
+    ids = torch.empty(hrows, dtype=torch.int64, device="cuda")
+    head.forward(torch.from_numpy(h).cuda(), hrows, logits, ids)
+    torch.cuda.synchronize()
+    shards = [None] * world
+    dist.all_gather_object(shards, logits.cpu().numpy())
+    if rank == 0:
+        full = np.concatenate(shards, axis=1)
+        results["err_head"] = rel_err(full, oracle.q_linear(14, hblocks, h, hrows, hk, vocab, threads=8))
+        results["head_ids_ok"] = ids.cpu().tolist() == [oracle.greedy_sample(r) for r in full]
         q.put(results)
     comm.close()
     dist.barrier()
@@ -191,7 +210,8 @@ def _run_world(world):
     alt = res["alternating"]
     assert alt["errs"] == (0, 0) and alt["same"] and alt["stable"]
     assert res["rows5"]["same"] and res["rows5"]["errs"] == (0, 0)
-    for key in ("err_o", "err_down", "err_rows5"):
+    assert res["head_ids_ok"]
+    for key in ("err_o", "err_down", "err_rows5", "err_head"):
         record_err(f"tp{world}.{key}", res[key])
         assert res[key] <= GEMV_RTOL, (key, res[key])
 
