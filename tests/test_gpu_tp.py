@@ -15,7 +15,8 @@ every rank's packet for its outputs has reached tag e + 1.
   of the 8B layer with no host synchronisation in between; every launch's
   output must be identical on all ranks and equal to the first launch of its
   kind, the final outputs must match the unsharded oracle, and no wait may
-  time out.
+  time out; the vocab-split Q6_K head (TPHead) must pick greedy_sample's id
+  over the gathered logits, which must match the oracle.
 """
 import ctypes as C
 import hashlib
