@@ -50,15 +50,13 @@ constexpr int kWarps = 8;   // warps per CTA
 // matrices, same-box A/B): for a single row, 4 stages beat 2 for Q4_K (2.3 KB
 // records) by 0.3-0.6 us per call; for Q6_K (3.3 KB records, 43 KB of planes
 // at K = 14336) more than 2 stages cost CTAs per SM and ran slower; Q8_0 units
-// are 4.3 KB; with two or more rows (bigger planes) 4 stages lost ~20%.
-#ifndef OCL_GEMV_STAGES_Q4
-#define OCL_GEMV_STAGES_Q4 4
-#endif
-#ifndef OCL_GEMV_STAGES
-#define OCL_GEMV_STAGES 2
-#endif
-__host__ __device__ constexpr int stages(int t, int nt) {
-    return (t == kQ4_K && nt == 0) ? OCL_GEMV_STAGES_Q4 : OCL_GEMV_STAGES;
+// are 4.3 KB; with two or more rows (bigger planes) 4 stages lost ~20%.  A
+// single-row Q4_K CTA whose K range exceeds 32 units (K = 14336: 43 KB of
+// planes) also runs 2 stages, which keeps two CTAs per SM: Q4_K 4096 x 14336
+// 11.7 -> 10.1 us (the same change cost 0.2-0.9 us at K = 4096).
+constexpr int kLongKUnits = 32;
+__host__ __device__ constexpr int stages(int t, int nt, int umax) {
+    return (t == kQ4_K && nt == 0 && umax <= kLongKUnits) ? 4 : 2;
 }
 
 __host__ __device__ constexpr int unit_bytes(int t) { return t == kQ4_K ? 2304 : t == kQ6_K ? 3360 : 4352; }
@@ -538,8 +536,8 @@ __host__ __device__ inline SmemMap smem_map(int type, int nt, int umax, int rows
     const int sstride = sum_per(type) ? umax * sum_per(type) / 2 + 4 : 0;
     SmemMap m;
     m.ring = 0;
-    m.bars = kWarps * stages(type, nt) * unit_bytes(type);
-    m.red = m.bars + (kWarps * stages(type, nt) + 2) * 8;              // +1 barrier for the planes, padded
+    m.bars = kWarps * stages(type, nt, umax) * unit_bytes(type);
+    m.red = m.bars + (kWarps * stages(type, nt, umax) + 2) * 8;              // +1 barrier for the planes, padded
     m.xq = (m.red + kWarps * 16 * rows * 4 + 127) & ~127;      // per-warp folded outputs
     m.xsum = m.xq + ncp * qstride;
     m.xs = m.xsum + ncp * sstride * 4;
@@ -713,10 +711,11 @@ __device__ __forceinline__ void gated_epilogue(const GemvArgs& a, const float* r
     if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
 }
 
-template <int TYPE, int NT, int EPI>
+template <int TYPE, int NT, int EPI, int S>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     // NT == 0: single activation row (planes in MMA columns 0, 2, 4)
-    constexpr int UB = unit_bytes(TYPE), S = stages(TYPE, NT), NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
+    // S (ring depth) = stages(TYPE, NT, a.umax), chosen by the host
+    constexpr int UB = unit_bytes(TYPE), NC = NT ? NT * 8 : 8, MPAD = NT ? (NC + 2) / 3 : 1;
     constexpr int NCP = NT ? 3 * MPAD : 3;  // plane rows copied from global
     constexpr int NTA = NT ? NT : 1;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -910,7 +909,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     }
 }
 
-template <int TYPE, int NT, int EPI>
+template <int TYPE, int NT, int EPI, int S>
 cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
     // Largest dynamic shared memory enabled so far, per template instance and
     // device (a function attribute is set per device).
@@ -919,7 +918,7 @@ cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaSt
     cudaGetDevice(&dev);
     size_t& configured = configured_by_dev[dev < kMaxDevices ? dev : 0];
     if (pl.smem > 48 * 1024 && (pl.smem > configured || dev >= kMaxDevices)) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT, EPI, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)pl.smem);
         if (e != cudaSuccess) return e;
         configured = pl.smem;
@@ -934,19 +933,21 @@ cudaError_t launch_typed(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT, EPI>, a);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, NT, EPI, S>, a);
 }
 
 template <int TYPE, int EPI>
 cudaError_t launch_nt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
     switch (pl.nt) {
-        case 0: return launch_typed<TYPE, 0, EPI>(pl, a, pdl, s);
-        case 1: return launch_typed<TYPE, 1, EPI>(pl, a, pdl, s);
-        case 2: return launch_typed<TYPE, 2, EPI>(pl, a, pdl, s);
-        case 3: return launch_typed<TYPE, 3, EPI>(pl, a, pdl, s);
-        case 4: return launch_typed<TYPE, 4, EPI>(pl, a, pdl, s);
-        case 5: return launch_typed<TYPE, 5, EPI>(pl, a, pdl, s);
-        case 6: return launch_typed<TYPE, 6, EPI>(pl, a, pdl, s);
+        case 0:
+            if (stages(TYPE, 0, pl.umax) == 4) return launch_typed<TYPE, 0, EPI, (TYPE == kQ4_K ? 4 : 2)>(pl, a, pdl, s);
+            return launch_typed<TYPE, 0, EPI, 2>(pl, a, pdl, s);
+        case 1: return launch_typed<TYPE, 1, EPI, 2>(pl, a, pdl, s);
+        case 2: return launch_typed<TYPE, 2, EPI, 2>(pl, a, pdl, s);
+        case 3: return launch_typed<TYPE, 3, EPI, 2>(pl, a, pdl, s);
+        case 4: return launch_typed<TYPE, 4, EPI, 2>(pl, a, pdl, s);
+        case 5: return launch_typed<TYPE, 5, EPI, 2>(pl, a, pdl, s);
+        case 6: return launch_typed<TYPE, 6, EPI, 2>(pl, a, pdl, s);
         default: return cudaErrorInvalidValue;
     }
 }
